@@ -1,0 +1,6 @@
+// binary_div.cu — instantiates the CTB_DIV dtype dispatch (see binary_impl.cuh).
+#include "binary_impl.cuh"
+
+namespace ctb {
+template int binary_dispatch<CTB_DIV>(const ctb_view*, const ctb_view*, const ctb_view*, cudaStream_t);
+}  // namespace ctb

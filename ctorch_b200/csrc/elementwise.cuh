@@ -1,0 +1,333 @@
+// elementwise.cuh — sm_100a elementwise kernels (binary, unary, fused binary chains).
+//
+// One functor `Fn` computes an output element from up to three input elements (each in its own
+// storage type; Fn converts). The planner (plan.cu) picks one of five launch shapes:
+//   Flat      rank 1 after collapsing, unit/zero strides: grid-stride 16-byte packs, 4 in flight
+//   RowsLong  unit/zero inner strides, rows >= 128 packs: CTA tiles of 1024 packs along a row,
+//             the row's base offsets decoded once per tile (FastDiv, no 64-bit divides)
+//   RowsShort same, short rows: each pack decodes its own row
+//   Tiled     one input read transposed (unit stride on an outer dim): 64x64 tile staged through
+//             shared memory so both the transposed read and the output write are coalesced
+//   General   anything else: per-element coordinate decode
+// Replaces ctorch's one-thread-per-element kernels (src/ops/binary_ops_cuda.cu:53-81,
+// src/ops/unary_ops_cuda.cu:50-75), which take a 64-bit div/mod per dim per element.
+#pragma once
+
+#include "common.cuh"
+#include "plan.cuh"
+
+namespace ctb {
+
+constexpr int kEwBlock = 256;
+constexpr int kEwUnroll = 4;
+constexpr int kTile = 64;
+
+struct NoIn {};
+
+template <class O, class I0, class I1, class I2, int NIN> constexpr int ew_vec() {
+    int m = sizeof(O);
+    if ((int)sizeof(I0) < m) m = sizeof(I0);
+    if (NIN > 1 && (int)sizeof(I1) < m) m = sizeof(I1);
+    if (NIN > 2 && (int)sizeof(I2) < m) m = sizeof(I2);
+    return 16 / m;
+}
+
+template <class Fn, class O, class I0, class I1, class I2, int NIN>
+__device__ __forceinline__ O ew_apply(const Fn& fn, I0 x0, I1 x1, I2 x2) {
+    if constexpr (NIN == 1) return fn(x0);
+    else if constexpr (NIN == 2) return fn(x0, x1);
+    else return fn(x0, x1, x2);
+}
+
+// Row base offsets for each operand: decode `row` over dims [0, rank-2] (outermost first).
+__device__ __forceinline__ void ew_decode_row(const EwArgs& p, uint64_t row, int nops,
+                                              int64_t* off) {
+    for (int o = 0; o < kMaxOps; ++o) off[o] = 0;
+    for (int d = p.rank - 2; d >= 0; --d) {
+        uint64_t q, r;
+        p.div[d].divmod(row, q, r);
+        for (int o = 0; o < nops; ++o) off[o] += static_cast<int64_t>(r) * p.stride[o][d];
+        row = q;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+template <class Fn, class O, class I0, class I1, class I2, int NIN>
+__global__ void __launch_bounds__(kEwBlock) ew_flat(EwArgs p, Fn fn) {
+    constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
+    constexpr int U = kEwUnroll;
+    O* __restrict__ out = static_cast<O*>(p.out);
+    const I0* __restrict__ in0 = static_cast<const I0*>(p.in[0]);
+    const I1* __restrict__ in1 = static_cast<const I1*>(p.in[1]);
+    const I2* __restrict__ in2 = static_cast<const I2*>(p.in[2]);
+    const bool b0 = p.stride[1][0] == 0;
+    const bool b1 = NIN > 1 && p.stride[2][0] == 0;
+    const bool b2 = NIN > 2 && p.stride[3][0] == 0;
+    const I0 s0 = b0 ? in0[0] : I0{};
+    I1 s1{};
+    I2 s2{};
+    if constexpr (NIN > 1) s1 = b1 ? in1[0] : I1{};
+    if constexpr (NIN > 2) s2 = b2 ? in2[0] : I2{};
+
+    const int64_t n = p.n;
+    const int64_t nvec = n / V;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t base = tid; base < nvec; base += nthr * U) {
+        Pack<I0, V> x0[U];
+        Pack<I1, V> x1[U];
+        Pack<I2, V> x2[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t v = base + u * nthr;
+            if (v < nvec) {
+                if (!b0) x0[u] = load_pack<I0, V>(in0 + v * V);
+                if constexpr (NIN > 1) if (!b1) x1[u] = load_pack<I1, V>(in1 + v * V);
+                if constexpr (NIN > 2) if (!b2) x2[u] = load_pack<I2, V>(in2 + v * V);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t v = base + u * nthr;
+            if (v < nvec) {
+                Pack<O, V> o;
+#pragma unroll
+                for (int e = 0; e < V; ++e)
+                    o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, b0 ? s0 : x0[u].v[e],
+                                                              b1 ? s1 : x1[u].v[e],
+                                                              b2 ? s2 : x2[u].v[e]);
+                store_pack<O, V>(out + v * V, o);
+            }
+        }
+    }
+    for (int64_t i = nvec * V + tid; i < n; i += nthr) {
+        out[i] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, in0[b0 ? 0 : i], NIN > 1 ? in1[b1 ? 0 : i] : I1{},
+                                                  NIN > 2 ? in2[b2 ? 0 : i] : I2{});
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+template <class Fn, class O, class I0, class I1, class I2, int NIN>
+__device__ __forceinline__ void ew_row_segment(const EwArgs& p, const Fn& fn, const int64_t* off,
+                                               int64_t c0, int64_t cstep, int count) {
+    constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
+    constexpr int U = kEwUnroll;
+    const int r = p.rank - 1;
+    O* __restrict__ out = static_cast<O*>(p.out) + off[0];
+    const I0* __restrict__ in0 = static_cast<const I0*>(p.in[0]) + off[1];
+    const I1* __restrict__ in1 = static_cast<const I1*>(p.in[1]) + off[2];
+    const I2* __restrict__ in2 = static_cast<const I2*>(p.in[2]) + off[3];
+    const bool b0 = p.stride[1][r] == 0;
+    const bool b1 = NIN > 1 && p.stride[2][r] == 0;
+    const bool b2 = NIN > 2 && p.stride[3][r] == 0;
+    const I0 s0 = b0 ? in0[0] : I0{};
+    I1 s1{};
+    I2 s2{};
+    if constexpr (NIN > 1) s1 = b1 ? in1[0] : I1{};
+    if constexpr (NIN > 2) s2 = b2 ? in2[0] : I2{};
+    Pack<I0, V> x0[U];
+    Pack<I1, V> x1[U];
+    Pack<I2, V> x2[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t c = c0 + u * cstep;
+        if (u < count && c < p.vpr) {
+            if (!b0) x0[u] = load_pack<I0, V>(in0 + c * V);
+            if constexpr (NIN > 1) if (!b1) x1[u] = load_pack<I1, V>(in1 + c * V);
+            if constexpr (NIN > 2) if (!b2) x2[u] = load_pack<I2, V>(in2 + c * V);
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t c = c0 + u * cstep;
+        if (u < count && c < p.vpr) {
+            Pack<O, V> o;
+#pragma unroll
+            for (int e = 0; e < V; ++e)
+                o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, b0 ? s0 : x0[u].v[e],
+                                                          b1 ? s1 : x1[u].v[e],
+                                                          b2 ? s2 : x2[u].v[e]);
+            store_pack<O, V>(out + c * V, o);
+        }
+    }
+}
+
+template <class Fn, class O, class I0, class I1, class I2, int NIN>
+__global__ void __launch_bounds__(kEwBlock) ew_rows_long(EwArgs p, Fn fn) {
+    const int64_t seg = static_cast<int64_t>(kEwBlock) * kEwUnroll;
+    const int64_t tiles = p.rows * static_cast<int64_t>(p.aux.d);
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        uint64_t row, s;
+        p.aux.divmod(static_cast<uint64_t>(t), row, s);
+        int64_t off[kMaxOps];
+        ew_decode_row(p, row, NIN + 1, off);
+        ew_row_segment<Fn, O, I0, I1, I2, NIN>(p, fn, off, static_cast<int64_t>(s) * seg + threadIdx.x,
+                                               kEwBlock, kEwUnroll);
+    }
+}
+
+template <class Fn, class O, class I0, class I1, class I2, int NIN>
+__global__ void __launch_bounds__(kEwBlock) ew_rows_short(EwArgs p, Fn fn) {
+    const int64_t nvec = p.rows * p.vpr;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t v = tid; v < nvec; v += nthr) {
+        uint64_t row, c;
+        p.aux.divmod(static_cast<uint64_t>(v), row, c);
+        int64_t off[kMaxOps];
+        ew_decode_row(p, row, NIN + 1, off);
+        ew_row_segment<Fn, O, I0, I1, I2, NIN>(p, fn, off, static_cast<int64_t>(c), 0, 1);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+template <class Fn, class O, class I0, class I1, class I2, int NIN>
+__global__ void __launch_bounds__(kEwBlock) ew_general(EwArgs p, Fn fn) {
+    O* __restrict__ out = static_cast<O*>(p.out);
+    const I0* __restrict__ in0 = static_cast<const I0*>(p.in[0]);
+    const I1* __restrict__ in1 = static_cast<const I1*>(p.in[1]);
+    const I2* __restrict__ in2 = static_cast<const I2*>(p.in[2]);
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = tid; i < p.n; i += nthr) {
+        uint64_t rem = static_cast<uint64_t>(i);
+        int64_t off[kMaxOps] = {0, 0, 0, 0};
+        for (int d = p.rank - 1; d >= 0; --d) {
+            uint64_t q, c;
+            p.div[d].divmod(rem, q, c);
+#pragma unroll
+            for (int o = 0; o <= NIN; ++o) off[o] += static_cast<int64_t>(c) * p.stride[o][d];
+            rem = q;
+        }
+        out[off[0]] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, in0[off[1]], NIN > 1 ? in1[off[2]] : I1{},
+                                                       NIN > 2 ? in2[off[3]] : I2{});
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Tiled: binary op where input XOP (1 or 2) has unit stride on dim p.pdim instead of the inner
+// dim. Each CTA stages a 64(p) x 64(l) tile of that input in shared memory, reading it along p
+// (coalesced), then writes output rows along l (coalesced).
+template <class Fn, class O, class I0, class I1, int XOP>
+__global__ void __launch_bounds__(kEwBlock) ew_tiled(EwArgs p, Fn fn) {
+    using X = std::conditional_t<XOP == 1, I0, I1>;
+    using Y = std::conditional_t<XOP == 1, I1, I0>;
+    constexpr int YOP = XOP == 1 ? 2 : 1;
+    __shared__ X tile[kTile][kTile + 1];
+    const int r = p.rank - 1;
+    const int pd = p.pdim;
+    const int64_t L = p.shape[r];
+    const int64_t P = p.shape[pd];
+    const int64_t sXl = p.stride[XOP][r];
+    const int64_t sYl = p.stride[YOP][r];
+    const int64_t sYp = p.stride[YOP][pd];
+    const int64_t sOp = p.stride[0][pd];
+    const X* __restrict__ xin = static_cast<const X*>(p.in[XOP - 1]);
+    const Y* __restrict__ yin = static_cast<const Y*>(p.in[YOP - 1]);
+    O* __restrict__ out = static_cast<O*>(p.out);
+    const int64_t tiles_l = static_cast<int64_t>(p.aux.d);
+    const int64_t tiles_p = static_cast<int64_t>(p.aux2.d);
+    const int64_t total = (p.n / (L * P)) * tiles_l * tiles_p;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        uint64_t rest, tl, batch, tp;
+        p.aux.divmod(static_cast<uint64_t>(t), rest, tl);
+        p.aux2.divmod(rest, batch, tp);
+        int64_t offO = 0, offX = 0, offY = 0;
+        for (int d = r - 1; d >= 0; --d) {
+            if (d == pd) continue;
+            uint64_t q, c;
+            p.div[d].divmod(batch, q, c);
+            offO += static_cast<int64_t>(c) * p.stride[0][d];
+            offX += static_cast<int64_t>(c) * p.stride[XOP][d];
+            offY += static_cast<int64_t>(c) * p.stride[YOP][d];
+            batch = q;
+        }
+        const int64_t l0 = static_cast<int64_t>(tl) * kTile;
+        const int64_t p0 = static_cast<int64_t>(tp) * kTile;
+        for (int k = threadIdx.x; k < kTile * kTile; k += kEwBlock) {
+            const int li = k >> 6, pi = k & 63;
+            const int64_t pp = p0 + pi, ll = l0 + li;
+            if (pp < P && ll < L) tile[li][pi] = xin[offX + pp + ll * sXl];
+        }
+        __syncthreads();
+        for (int k = threadIdx.x; k < kTile * kTile; k += kEwBlock) {
+            const int pi = k >> 6, li = k & 63;
+            const int64_t pp = p0 + pi, ll = l0 + li;
+            if (pp < P && ll < L) {
+                const X x = tile[li][pi];
+                const Y y = yin[offY + pp * sYp + ll * sYl];
+                O o;
+                if constexpr (XOP == 1) o = fn(x, y);
+                else o = fn(y, x);
+                out[offO + pp * sOp + ll] = o;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Launcher. Returns a ctb_status.
+template <class Fn, class O, class I0, class I1 = I0, class I2 = I0, int NIN = 1>
+int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
+    constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
+    const EwArgs& a = plan.args;
+    switch (plan.path) {
+    case EwPath::Empty:
+        return CTB_OK;
+    case EwPath::Flat: {
+        const int64_t nvec = a.n / V;
+        const int64_t work = (nvec + kEwBlock * kEwUnroll - 1) / (kEwBlock * kEwUnroll);
+        ew_flat<Fn, O, I0, I1, I2, NIN><<<grid_for(work < 1 ? 1 : work, 16), kEwBlock, 0, st>>>(a, fn);
+        break;
+    }
+    case EwPath::RowsLong: {
+        const int64_t tiles = a.rows * static_cast<int64_t>(a.aux.d);
+        ew_rows_long<Fn, O, I0, I1, I2, NIN><<<grid_for(tiles, 16), kEwBlock, 0, st>>>(a, fn);
+        break;
+    }
+    case EwPath::RowsShort: {
+        const int64_t nvec = a.rows * a.vpr;
+        ew_rows_short<Fn, O, I0, I1, I2, NIN><<<grid_for((nvec + kEwBlock - 1) / kEwBlock, 16), kEwBlock, 0, st>>>(a, fn);
+        break;
+    }
+    case EwPath::Tiled: {
+        if constexpr (NIN == 2) {
+            const int64_t L = a.shape[a.rank - 1];
+            const int64_t P = a.shape[a.pdim];
+            const int64_t total = (a.n / (L * P)) * static_cast<int64_t>(a.aux.d) * static_cast<int64_t>(a.aux2.d);
+            if (a.xop == 1)
+                ew_tiled<Fn, O, I0, I1, 1><<<grid_for(total, 16), kEwBlock, 0, st>>>(a, fn);
+            else
+                ew_tiled<Fn, O, I0, I1, 2><<<grid_for(total, 16), kEwBlock, 0, st>>>(a, fn);
+            break;
+        }
+        [[fallthrough]];
+    }
+    case EwPath::General: {
+        ew_general<Fn, O, I0, I1, I2, NIN><<<grid_for((a.n + kEwBlock - 1) / kEwBlock, 16), kEwBlock, 0, st>>>(a, fn);
+        break;
+    }
+    }
+    count_launch();
+    return check_launch("elementwise");
+}
+
+// ------------------------------------------------------------------------------------------------
+// Functors
+
+template <int OP, class O> struct FnBinary {
+    template <class A, class B> __device__ __forceinline__ O operator()(A a, B b) const {
+        return BinOp<OP>::template apply<O>(cvt<O>(a), cvt<O>(b));
+    }
+};
+
+// op2(op1(a, b) rounded to M, c) rounded to O.
+template <int OP1, int OP2, class M, class O> struct FnChain {
+    template <class A, class B, class C> __device__ __forceinline__ O operator()(A a, B b, C c) const {
+        const M m = BinOp<OP1>::template apply<M>(cvt<M>(a), cvt<M>(b));
+        return BinOp<OP2>::template apply<O>(cvt<O>(m), cvt<O>(c));
+    }
+};
+
+}  // namespace ctb

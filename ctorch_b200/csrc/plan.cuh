@@ -1,0 +1,129 @@
+// plan.cuh — host-side iteration planning: broadcast, dim collapse, and the choice between the
+// vectorised, row, tiled-transpose and general kernels. Replaces ctorch's BinaryIndexer /
+// ReductionPlan construction (src/ops/tensor_iter.cpp:41-84, src/ops/reduction_iter.cpp:20-69)
+// for the CUDA side: instead of handing a rank-16 odometer to every thread, the planner collapses
+// the iteration space first and picks a kernel shaped for what is left.
+#pragma once
+
+#include "common.cuh"
+
+namespace ctb {
+
+// Elementwise iteration space over up to 4 operands (0 = out, 1..3 = inputs).
+constexpr int kMaxOps = 4;
+
+enum class EwPath : int { Empty = 0, Flat = 1, RowsLong = 2, RowsShort = 3, Tiled = 4, General = 5 };
+
+struct EwSpace {
+    int nops = 0;  // out + inputs
+    int rank = 0;
+    int64_t shape[kMaxDims] = {};
+    int64_t stride[kMaxOps][kMaxDims] = {};
+    int64_t numel() const {
+        int64_t n = 1;
+        for (int d = 0; d < rank; ++d) n *= shape[d];
+        return n;
+    }
+};
+
+// Right-aligned broadcast of `v` to (rank, shape): size-1 and missing dims get stride 0
+// (src/ops/broadcast.cpp:35-82). Returns false if the shapes do not broadcast.
+bool broadcast_strides(const ctb_view& v, int rank, const int64_t* shape, int64_t* strides);
+
+// Drops size-1 dims and merges adjacent dims whose strides chain for every operand
+// (stride[d] == stride[d+1] * shape[d+1]). Keeps the order of out's dims. A 0-d space becomes
+// rank 1 with shape [1].
+void collapse(EwSpace& s);
+
+// Kernel parameters shared by the elementwise kernels (passed by value, lives in the constant
+// bank). Dims are stored outermost-first, as in ctorch.
+struct EwArgs {
+    void* out;
+    const void* in[3];
+    int rank;
+    int xop;                       // Tiled: which input (1..3) is read transposed
+    int pdim;                      // Tiled: the dim on which that input has stride 1
+    int64_t n;                     // total elements
+    int64_t L;                     // innermost extent
+    int64_t rows;                  // n / L
+    int64_t vpr;                   // vectors per row (RowsLong/RowsShort)
+    int64_t shape[kMaxDims];
+    int64_t stride[kMaxOps][kMaxDims];
+    FastDiv div[kMaxDims];         // divisors = shape[d]
+    FastDiv aux;                   // RowsLong: segments per row; RowsShort: vectors per row;
+                                   // Tiled: tiles along L
+    FastDiv aux2;                  // Tiled: tiles along P
+};
+
+struct EwPlan {
+    EwPath path = EwPath::Empty;
+    int vec = 1;
+    EwSpace space;
+    EwArgs args;
+};
+
+// Plans out = f(in...) given the operand views (already validated for dtype). `vec` is the number
+// of elements one 16-byte pack holds for the narrowest participating type.
+int plan_elementwise(const ctb_view* out, const ctb_view* const* ins, int nin, const int* sizes,
+                     int vec, EwPlan& plan);
+
+const char* ew_path_name(EwPath p);
+
+// ------------------------------------------------------------------------------------------------
+// Reductions: a kept space (one output each) and a reduced space, both collapsed.
+
+enum class RedPath : int { Empty = 0, Inner = 1, Outer = 2, General = 3 };
+
+struct RedSpace {
+    int rank_k = 0, rank_r = 0;
+    int64_t shape_k[kMaxDims] = {}, stride_k[kMaxDims] = {}, stride_o[kMaxDims] = {};
+    int64_t stride_o2[kMaxDims] = {};  // second output (indices) for the with-index reductions
+    int64_t shape_r[kMaxDims] = {}, stride_r[kMaxDims] = {};
+    int64_t kept = 1, red = 1;
+};
+
+struct RedArgs {
+    const void* in;
+    void* out;   // values (or sum/mean/prod result)
+    void* out2;  // indices (with-index reductions)
+    void* scratch;
+    int rank_k, rank_r;
+    int split;          // S: CTAs that share one output's reduced range (1 = no combine pass)
+    int64_t kept, red;  // numels
+    int64_t chunk;      // reduced elements per split
+    int64_t N;          // Outer: contiguous kept extent
+    int64_t K;          // Outer: reduced extent; Inner: row length
+    int64_t strideK;    // Outer: stride of the reduced dim
+    int64_t shape_k[kMaxDims], stride_k[kMaxDims], stride_o[kMaxDims], stride_o2[kMaxDims];
+    int64_t shape_r[kMaxDims], stride_r[kMaxDims];
+    FastDiv div_k[kMaxDims];
+    FastDiv div_r[kMaxDims];
+    FastDiv aux;        // Outer: column tiles; Inner: splits
+    FastDiv aux2;       // Outer: splits
+};
+
+struct RedPlan {
+    RedPath path = RedPath::Empty;
+    RedSpace space;
+    RedArgs args;
+    int block = 256;
+    unsigned grid = 1;
+    bool warp_rows = false;  // Inner: one warp per row instead of one CTA per row
+    int col_tile = 0;        // Outer: columns per CTA
+};
+
+// Builds the kept/reduced split of `in` for the given mask and output view(s) (out2 may be null),
+// collapses each half, and classifies it. Output strides follow ctorch's rule: with keepdim
+// (out rank == in rank) every input dim has an output slot, otherwise only kept dims do
+// (src/ops/reduction_iter.cpp:20-69).
+int plan_reduction(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint32_t mask,
+                   RedPlan& plan);
+
+// Chooses split counts / grid for a planned reduction. `state_bytes` is the size of one partial
+// state, `outer_vec` the column-strip pack width the Outer kernel will use; returns the scratch
+// bytes the plan needs.
+size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int outer_vec);
+
+const char* red_path_name(RedPath p);
+
+}  // namespace ctb

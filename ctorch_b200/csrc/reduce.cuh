@@ -1,0 +1,482 @@
+// reduce.cuh — sm_100a reduction kernels (sum / mean / prod / max / min, with or without indices).
+//
+// A reducer R supplies State, init(), fold(state, value, position), combine(state, state) and
+// write(). Kernels (chosen by plan_reduction / finish_reduction_plan in plan.cu):
+//   red_inner_cta   reduced range contiguous (row reductions, whole-tensor sums): one CTA per
+//                   (row, split), 16-byte loads four deep, warp-shuffle then shared-memory tree
+//   red_inner_warp  same for short rows: one warp per row
+//   red_outer       reduced dim strided, kept dim contiguous (column reductions): each warp walks
+//                   rows of a 32*V-column strip, warps combine through shared memory
+//   red_general_*   any other layout: per-element coordinate decode
+//   red_finalize    deterministic fixed-order combine of split partials (the second pass)
+// Replaces ctorch's one-thread-per-output axis kernels and whole-tensor two-pass kernels
+// (src/ops/reduction_ops_cuda.cu:92-350).
+//
+// Determinism and parity: every combine order is fixed by the launch shape, which depends only
+// on the problem size and the SM count, so results are run-to-run identical. Integer sums and
+// products accumulate in uint64 (two's-complement wrap, identical to any order); float sums and
+// products accumulate in double; max/min carry the element's position so ties resolve to the
+// first occurrence and NaN to the first NaN, exactly as the sequential CPU fold
+// (src/ops/reduction_functors.h:55-110, src/ops/reduction_ops_cpu.cpp:236-297).
+#pragma once
+
+#include <limits>
+
+#include "common.cuh"
+#include "plan.cuh"
+
+namespace ctb {
+
+constexpr int kRedBlock = 256;
+constexpr int kRedUnroll = 4;
+
+// ------------------------------------------------------------------------------------------------
+// shuffles
+
+template <class T> __device__ __forceinline__ T shfl_xor(T v, int m) {
+    if constexpr (std::is_same_v<T, uint8_t>) {
+        return static_cast<uint8_t>(__shfl_xor_sync(0xffffffffu, static_cast<int>(v), m));
+    } else if constexpr (std::is_same_v<T, int64_t>) {
+        return static_cast<int64_t>(__shfl_xor_sync(0xffffffffu, static_cast<long long>(v), m));
+    } else if constexpr (std::is_same_v<T, uint64_t>) {
+        return static_cast<uint64_t>(
+            __shfl_xor_sync(0xffffffffu, static_cast<unsigned long long>(v), m));
+    } else {
+        return __shfl_xor_sync(0xffffffffu, v, m);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// reducers
+
+// Sum / product with a widening accumulator: double for float inputs, uint64 (wrapping) for
+// integer and bool inputs (src/ops/reduction_ops_cpu.cpp:98-152).
+template <class T, bool IsProd> struct RAccum {
+    using In = T;
+    using State = std::conditional_t<is_float_v<T>, double, uint64_t>;
+    using Out = std::conditional_t<is_float_v<T>, T, int64_t>;
+    __device__ __forceinline__ static State init() { return IsProd ? State(1) : State(0); }
+    __device__ __forceinline__ static State conv(T v) {
+        if constexpr (is_float_v<T>) return static_cast<double>(v);
+        else if constexpr (std::is_same_v<T, uint8_t>) return static_cast<uint64_t>(v);
+        else return static_cast<uint64_t>(static_cast<int64_t>(v));
+    }
+    __device__ __forceinline__ static void combine(State& a, State b) {
+        if constexpr (is_float_v<T>) a = IsProd ? __dmul_rn(a, b) : __dadd_rn(a, b);
+        else a = IsProd ? a * b : a + b;
+    }
+    __device__ __forceinline__ static void fold(State& s, T v, int64_t) { combine(s, conv(v)); }
+    __device__ __forceinline__ static State shfl(State s, int m) { return shfl_xor(s, m); }
+    __device__ __forceinline__ static void write(const RedArgs& p, const State& s, int64_t o1, int64_t) {
+        if constexpr (is_float_v<T>) static_cast<T*>(p.out)[o1] = static_cast<T>(s);
+        else static_cast<int64_t*>(p.out)[o1] = static_cast<int64_t>(s);
+    }
+};
+
+// mean = T(sum) then *= T(1)/T(N); NaN (ctorch's quiet_NaN bits) when N == 0
+// (src/ops/reduction_ops_cpu.cpp:160-175).
+template <class T> struct RMean : RAccum<T, false> {
+    using Base = RAccum<T, false>;
+    using State = typename Base::State;
+    __device__ __forceinline__ static void write(const RedArgs& p, const State& s, int64_t o1, int64_t) {
+        T o;
+        if (p.red == 0) {
+            if constexpr (std::is_same_v<T, float>) o = __int_as_float(0x7fc00000);
+            else o = __longlong_as_double(0x7ff8000000000000LL);
+        } else {
+            o = static_cast<T>(s);
+            if constexpr (std::is_same_v<T, float>)
+                o = __fmul_rn(o, __fdiv_rn(1.0f, static_cast<float>(p.red)));
+            else
+                o = __dmul_rn(o, __ddiv_rn(1.0, static_cast<double>(p.red)));
+        }
+        static_cast<T*>(p.out)[o1] = o;
+    }
+};
+
+// Sum of a float shard into a double partial (multi-GPU whole-tensor sum).
+template <class T> struct RSumPartial : RAccum<T, false> {
+    using State = typename RAccum<T, false>::State;
+    __device__ __forceinline__ static void write(const RedArgs& p, const State& s, int64_t o1, int64_t) {
+        static_cast<double*>(p.out)[o1] = s;
+    }
+};
+
+template <class T> struct MMState {
+    T v;
+    int64_t i;
+};
+
+// max / min carrying the position: NaN beats numbers (first NaN wins), then the larger (smaller)
+// value, then the smaller position. Equivalent to ctorch's sequential strict-compare fold.
+template <class T, bool IsMax, bool Indexed> struct RMinMax {
+    using In = T;
+    using State = MMState<T>;
+    __device__ __forceinline__ static T ident() {
+        if constexpr (is_float_v<T>)
+            return IsMax ? -std::numeric_limits<T>::infinity() : std::numeric_limits<T>::infinity();
+        else
+            return IsMax ? std::numeric_limits<T>::lowest() : std::numeric_limits<T>::max();
+    }
+    __device__ __forceinline__ static State init() {
+        return State{ident(), std::numeric_limits<int64_t>::max()};
+    }
+    __device__ __forceinline__ static bool better(const State& a, T bv, int64_t bi) {
+        if constexpr (is_float_v<T>) {
+            const bool an = a.v != a.v, bn = bv != bv;
+            if (an | bn) return an ? (bn && bi < a.i) : true;
+        }
+        if (IsMax ? (bv > a.v) : (bv < a.v)) return true;
+        return bv == a.v && bi < a.i;
+    }
+    __device__ __forceinline__ static void fold(State& s, T v, int64_t j) {
+        if (better(s, v, j)) {
+            s.v = v;
+            s.i = j;
+        }
+    }
+    __device__ __forceinline__ static void combine(State& a, const State& b) { fold(a, b.v, b.i); }
+    __device__ __forceinline__ static State shfl(const State& s, int m) {
+        return State{shfl_xor(s.v, m), shfl_xor(s.i, m)};
+    }
+    __device__ __forceinline__ static void write(const RedArgs& p, const State& s, int64_t o1, int64_t o2) {
+        if (p.out) static_cast<T*>(p.out)[o1] = s.v;
+        if constexpr (Indexed) static_cast<int64_t*>(p.out2)[o2] = s.i;
+    }
+};
+
+// ------------------------------------------------------------------------------------------------
+// helpers
+
+template <class R> __device__ __forceinline__ typename R::State warp_reduce(typename R::State s) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) R::combine(s, R::shfl(s, m));
+    return s;
+}
+
+// Result valid in thread 0. `smem` holds one State per warp.
+template <class R> __device__ __forceinline__ typename R::State block_reduce(typename R::State s,
+                                                                             typename R::State* smem) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    s = warp_reduce<R>(s);
+    if (lane == 0) smem[warp] = s;
+    __syncthreads();
+    if (warp == 0) {
+        s = lane < nwarps ? smem[lane] : R::init();
+        s = warp_reduce<R>(s);
+    }
+    __syncthreads();
+    return s;
+}
+
+// Offsets of kept index k: input, first output, second output.
+__device__ __forceinline__ void red_decode_kept(const RedArgs& p, uint64_t k, int64_t& in_off,
+                                                int64_t& o1, int64_t& o2) {
+    in_off = o1 = o2 = 0;
+    for (int d = p.rank_k - 1; d >= 0; --d) {
+        uint64_t q, c;
+        p.div_k[d].divmod(k, q, c);
+        in_off += static_cast<int64_t>(c) * p.stride_k[d];
+        o1 += static_cast<int64_t>(c) * p.stride_o[d];
+        o2 += static_cast<int64_t>(c) * p.stride_o2[d];
+        k = q;
+    }
+}
+
+__device__ __forceinline__ int64_t red_decode_red(const RedArgs& p, uint64_t j) {
+    int64_t off = 0;
+    for (int d = p.rank_r - 1; d >= 0; --d) {
+        uint64_t q, c;
+        p.div_r[d].divmod(j, q, c);
+        off += static_cast<int64_t>(c) * p.stride_r[d];
+        j = q;
+    }
+    return off;
+}
+
+// Folds row[j] for j in [j0, j1) into s, elements spread over nthr threads: scalar head up to
+// the first 16-byte boundary, 16-byte packs kRedUnroll deep, scalar tail.
+template <class R> __device__ __forceinline__ void fold_contig(const typename R::In* row, int64_t j0,
+                                                               int64_t j1, typename R::State& s,
+                                                               int tid, int nthr) {
+    using T = typename R::In;
+    constexpr int V = 16 / sizeof(T);
+    constexpr int U = kRedUnroll;
+    if (j1 <= j0) return;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(row + j0);
+    const int64_t head = static_cast<int64_t>(((16u - (addr & 15u)) & 15u) / sizeof(T));
+    const int64_t jh = j0 + head < j1 ? j0 + head : j1;
+    for (int64_t j = j0 + tid; j < jh; j += nthr) R::fold(s, row[j], j);
+    const int64_t nv = (j1 - jh) / V;
+    const T* body = row + jh;
+    for (int64_t v = tid; v < nv; v += static_cast<int64_t>(nthr) * U) {
+        Pack<T, V> x[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t w = v + static_cast<int64_t>(u) * nthr;
+            if (w < nv) x[u] = load_pack<T, V>(body + w * V);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t w = v + static_cast<int64_t>(u) * nthr;
+            if (w < nv) {
+#pragma unroll
+                for (int e = 0; e < V; ++e) R::fold(s, x[u].v[e], jh + w * V + e);
+            }
+        }
+    }
+    for (int64_t j = jh + nv * V + tid; j < j1; j += nthr) R::fold(s, row[j], j);
+}
+
+// ------------------------------------------------------------------------------------------------
+// kernels
+
+template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_cta(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    __shared__ S smem[32];
+    const int64_t total = p.kept * p.split;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        uint64_t row, sp;
+        p.aux.divmod(static_cast<uint64_t>(t), row, sp);
+        int64_t in_off, o1, o2;
+        red_decode_kept(p, row, in_off, o1, o2);
+        const T* base = static_cast<const T*>(p.in) + in_off;
+        const int64_t j0 = static_cast<int64_t>(sp) * p.chunk;
+        const int64_t j1 = j0 + p.chunk < p.K ? j0 + p.chunk : p.K;
+        S st = R::init();
+        fold_contig<R>(base, j0, j1, st, threadIdx.x, blockDim.x);
+        st = block_reduce<R>(st, smem);
+        if (threadIdx.x == 0) {
+            if (p.split == 1) R::write(p, st, o1, o2);
+            else static_cast<S*>(p.scratch)[t] = st;
+        }
+    }
+}
+
+template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_warp(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t row = warp; row < p.kept; row += nwarps) {
+        int64_t in_off, o1, o2;
+        red_decode_kept(p, static_cast<uint64_t>(row), in_off, o1, o2);
+        S st = R::init();
+        fold_contig<R>(static_cast<const T*>(p.in) + in_off, 0, p.K, st, lane, 32);
+        st = warp_reduce<R>(st);
+        if (lane == 0) R::write(p, st, o1, o2);
+    }
+}
+
+// Column strips: kept inner dim N contiguous, reduced dim K with stride strideK, batch dims in
+// front. CTA = 8 warps; warp w folds rows k0+w, k0+w+8, ... of a 32*V-column strip.
+template <class R, int V> __global__ void __launch_bounds__(kRedBlock) red_outer(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    constexpr int W = kRedBlock / 32;
+    constexpr int U = kRedUnroll;
+    __shared__ S smem[W - 1][32 * V];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t tiles_n = static_cast<int64_t>(p.aux.d);
+    const int64_t total = (p.kept / p.N) * tiles_n * p.split;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        uint64_t rest, sp, b, tn;
+        p.aux2.divmod(static_cast<uint64_t>(t), rest, sp);
+        p.aux.divmod(rest, b, tn);
+        int64_t in_off = 0, o1 = 0, o2 = 0;
+        {
+            uint64_t bb = b;
+            for (int d = p.rank_k - 2; d >= 0; --d) {
+                uint64_t q, c;
+                p.div_k[d].divmod(bb, q, c);
+                in_off += static_cast<int64_t>(c) * p.stride_k[d];
+                o1 += static_cast<int64_t>(c) * p.stride_o[d];
+                o2 += static_cast<int64_t>(c) * p.stride_o2[d];
+                bb = q;
+            }
+        }
+        const int64_t col0 = static_cast<int64_t>(tn) * (32 * V) + lane * V;
+        const int64_t k0 = static_cast<int64_t>(sp) * p.chunk;
+        const int64_t k1 = k0 + p.chunk < p.K ? k0 + p.chunk : p.K;
+        S st[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) st[e] = R::init();
+        const T* base = static_cast<const T*>(p.in) + in_off + col0;
+        if (col0 + V <= p.N) {
+            for (int64_t k = k0 + warp; k < k1; k += W * U) {
+                Pack<T, V> x[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t kk = k + u * W;
+                    if (kk < k1) x[u] = load_pack<T, V>(base + kk * p.strideK);
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t kk = k + u * W;
+                    if (kk < k1) {
+#pragma unroll
+                        for (int e = 0; e < V; ++e) R::fold(st[e], x[u].v[e], kk);
+                    }
+                }
+            }
+        } else {
+            for (int64_t k = k0 + warp; k < k1; k += W) {
+#pragma unroll
+                for (int e = 0; e < V; ++e)
+                    if (col0 + e < p.N) R::fold(st[e], base[k * p.strideK + e], k);
+            }
+        }
+        if (warp > 0) {
+#pragma unroll
+            for (int e = 0; e < V; ++e) smem[warp - 1][lane * V + e] = st[e];
+        }
+        __syncthreads();
+        if (warp == 0) {
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                for (int w = 0; w < W - 1; ++w) R::combine(st[e], smem[w][lane * V + e]);
+                const int64_t col = col0 + e;
+                if (col < p.N) {
+                    if (p.split == 1) {
+                        R::write(p, st[e], o1 + col, o2 + col);
+                    } else {
+                        const int64_t k = static_cast<int64_t>(b) * p.N + col;
+                        static_cast<S*>(p.scratch)[k * p.split + static_cast<int64_t>(sp)] = st[e];
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// One thread per output, folding the reduced subspace in row-major order (the CPU's order).
+template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_thread(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const T* in = static_cast<const T*>(p.in);
+    for (int64_t k = tid; k < p.kept; k += nthr) {
+        int64_t in_off, o1, o2;
+        red_decode_kept(p, static_cast<uint64_t>(k), in_off, o1, o2);
+        S st = R::init();
+        for (int64_t j = 0; j < p.red; ++j) R::fold(st, in[in_off + red_decode_red(p, j)], j);
+        R::write(p, st, o1, o2);
+    }
+}
+
+// CTAs share one output's reduced range (few outputs, long strided reductions).
+template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_cta(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    __shared__ S smem[32];
+    const T* in = static_cast<const T*>(p.in);
+    const int64_t total = p.kept * p.split;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        uint64_t k, sp;
+        p.aux.divmod(static_cast<uint64_t>(t), k, sp);
+        int64_t in_off, o1, o2;
+        red_decode_kept(p, k, in_off, o1, o2);
+        const int64_t j0 = static_cast<int64_t>(sp) * p.chunk;
+        const int64_t j1 = j0 + p.chunk < p.red ? j0 + p.chunk : p.red;
+        S st = R::init();
+        for (int64_t j = j0 + threadIdx.x; j < j1; j += blockDim.x)
+            R::fold(st, in[in_off + red_decode_red(p, static_cast<uint64_t>(j))], j);
+        st = block_reduce<R>(st, smem);
+        if (threadIdx.x == 0) {
+            if (p.split == 1) R::write(p, st, o1, o2);
+            else static_cast<S*>(p.scratch)[t] = st;
+        }
+    }
+}
+
+// Second pass: combine the `split` partials of each output in split order.
+template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize(RedArgs p) {
+    using S = typename R::State;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const S* part = static_cast<const S*>(p.scratch);
+    for (int64_t k = tid; k < p.kept; k += nthr) {
+        S st = part[k * p.split];
+        for (int s = 1; s < p.split; ++s) R::combine(st, part[k * p.split + s]);
+        int64_t in_off, o1, o2;
+        red_decode_kept(p, static_cast<uint64_t>(k), in_off, o1, o2);
+        R::write(p, st, o1, o2);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// launcher
+
+template <class R>
+int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t need,
+                     cudaStream_t st) {
+    RedArgs& a = plan.args;
+    if (plan.path == RedPath::Empty) return CTB_OK;
+    if (need > 0) {
+        if (scratch == nullptr || scratch_bytes < need)
+            return fail(CTB_ERR_SCRATCH, "scratch buffer too small: need " + std::to_string(need) +
+                                             " bytes, got " + std::to_string(scratch_bytes));
+        a.scratch = scratch;
+    }
+    int launches = 1;
+    switch (plan.path) {
+    case RedPath::Inner:
+        if (plan.warp_rows) red_inner_warp<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+        else red_inner_cta<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+        break;
+    case RedPath::Outer: {
+        using T = typename R::In;
+        constexpr int VMAX = sizeof(T) >= 8 ? 2 : 4;
+        if (plan.col_tile == 32 * VMAX) red_outer<R, VMAX><<<plan.grid, kRedBlock, 0, st>>>(a);
+        else red_outer<R, 1><<<plan.grid, kRedBlock, 0, st>>>(a);
+        break;
+    }
+    case RedPath::General:
+        if (plan.warp_rows) red_general_thread<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+        else red_general_cta<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+        break;
+    default:
+        break;
+    }
+    if (a.split > 1) {
+        red_finalize<R><<<grid_for((a.kept + kRedBlock - 1) / kRedBlock, 8), kRedBlock, 0, st>>>(a);
+        ++launches;
+    }
+    count_launch(launches);
+    return check_launch("reduction");
+}
+
+// Outer-path vector width the kernels use for element type T (see launch_reduction).
+template <class T> constexpr int outer_vec() { return sizeof(T) >= 8 ? 2 : 4; }
+
+// Whether the Outer strip kernel may use V-wide loads for this plan.
+inline bool outer_vec_ok(const RedPlan& plan, int elem_bytes, int V) {
+    const RedArgs& a = plan.args;
+    if (plan.path != RedPath::Outer) return false;
+    const int bytes = elem_bytes * V;
+    if (reinterpret_cast<uintptr_t>(a.in) % bytes) return false;
+    if (a.N % V || a.strideK % V) return false;
+    for (int d = 0; d < a.rank_k - 1; ++d)
+        if (a.stride_k[d] % V) return false;
+    return true;
+}
+
+// Plans + sizes a reduction for reducer R; returns scratch bytes via `need`.
+template <class R>
+int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint32_t mask,
+             RedPlan& plan, size_t& need) {
+    using T = typename R::In;
+    int rc = plan_reduction(in, out, out2, mask, plan);
+    if (rc) return rc;
+    constexpr int V = outer_vec<T>();
+    const bool vec_ok = outer_vec_ok(plan, sizeof(T), V);
+    need = finish_reduction_plan(plan, sizeof(T), sizeof(typename R::State), vec_ok ? V : 1);
+    return CTB_OK;
+}
+
+}  // namespace ctb

@@ -1,0 +1,33 @@
+/*
+ * ctb_debug.h — host-only introspection of the B200 backend's planner. These functions make no
+ * CUDA call that needs a device, so the planner can be tested on a machine without a GPU. They
+ * have no counterpart in ctorch (ctorch builds its iteration plans inline:
+ * src/ops/tensor_iter.cpp:41-84, src/ops/reduction_iter.cpp:20-69).
+ */
+#ifndef CTB_CTB_DEBUG_H
+#define CTB_CTB_DEBUG_H
+
+#include "ctb/ctb.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Plans out = f(ins...) as ctb_binary / ctb_unary / ctb_binary_chain would and reports the launch
+ * shape ("empty", "flat", "rows_long", "rows_short", "tiled", "general"), the collapsed rank and
+ * the collapsed shape (shape must hold 16 entries). `vec` is the pack width in elements. */
+CTB_API int ctb_debug_plan_elementwise(const ctb_view* out, const ctb_view* const* ins, int nin, int vec,
+                               char* path, int path_len, int* rank, int64_t* shape);
+
+/* Plans a reduction and reports "empty", "inner", "outer" or "general" and the collapsed ranks. */
+CTB_API int ctb_debug_plan_reduction(const ctb_view* in, const ctb_view* out, uint32_t reduce_mask,
+                             char* path, int path_len, int* rank_kept, int* rank_red);
+
+/* floor(n / d) through the kernels' invariant-divisor multiply (n < 2^63, d >= 1). */
+CTB_API uint64_t ctb_debug_fastdiv(uint64_t n, uint64_t d);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CTB_CTB_DEBUG_H */

@@ -1,0 +1,321 @@
+"""Every launch shape of the CUDA backend against the oracle (oracle/ctb_oracle.c) on seeded
+inputs large enough to exercise it: the flat / row / short-row / tiled-transpose / general
+elementwise kernels, every promoted dtype pair, the fused chain, the inner (CTA, warp, split) /
+outer (split) / general reduction kernels with NaN, ties and signed zeros, and the row / general
+gathers. Same parity bar as test_gpu_golden.py."""
+import zlib
+
+import numpy as np
+import pytest
+
+from catalog import apply_numpy, apply_torch
+from helpers import TOL_SUM, assert_bitexact, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _seed(*parts) -> int:
+    return zlib.crc32(repr(parts).encode())
+
+
+def _pair(base: np.ndarray, recipe=()):
+    import torch
+
+    t = apply_torch(torch.from_numpy(np.ascontiguousarray(base)).cuda(), list(recipe))
+    return apply_numpy(base, list(recipe)), t
+
+
+def _rand(rng, shape, dt):
+    dt = np.dtype(dt)
+    if dt.kind == "f":
+        return rng.standard_normal(shape).astype(dt)
+    if dt == np.bool_:
+        return rng.integers(0, 2, shape).astype(np.bool_)
+    return rng.integers(-1000, 1000, shape).astype(dt)
+
+
+BIN_LAYOUTS = {
+    # name: (shape_a, recipe_a, shape_b, recipe_b)
+    "flat_tail": ((1_000_003,), [], (1_000_003,), []),
+    "flat_scalar": ((777_777,), [], (), []),
+    "rows_long": ((384, 4096), [], (1, 4096), []),
+    "rows_long_col": ((300, 8192), [], (300, 1), []),
+    "rows_short": ((20_000, 12), [], (1, 12), []),
+    "rows_short_3d": ((50, 40, 8), [], (40, 1), []),
+    "tiled": ((6, 200, 300), [], (6, 300, 200), [("permute", [0, 2, 1])]),
+    "tiled_lhs": ((4, 130, 70), [("permute", [0, 2, 1])], (4, 70, 130), []),
+    "general_offset": ((513, 257), [("slice", 0, 1, 513, 1)], (257,), []),
+    "general_step": ((300, 200), [("slice", 1, 0, 200, 3)], (300, 1), []),
+    "general_select": ((40, 7, 300), [("select", 1, 3)], (40, 300), [("slice", 1, 0, 300, 1)]),
+}
+
+
+@pytest.mark.parametrize("layout", sorted(BIN_LAYOUTS))
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div"])
+def test_binary_layouts_f32(cuda_ok, oracle, op, layout):
+    import ctorch_b200 as cb
+
+    rng = np.random.default_rng(_seed(op, layout))
+    sa, ra, sb, rb = BIN_LAYOUTS[layout]
+    a, ta = _pair(_rand(rng, sa, np.float32), ra)
+    b, tb = _pair(_rand(rng, sb, np.float32), rb)
+    got = getattr(cb, op)(ta, tb).cpu().numpy()
+    assert_bitexact(got, oracle.binary(op, a, b), f"{op} {layout}", nan_payload=False)
+
+
+DTYPE_PAIRS = [
+    (np.int32, np.int32), (np.int64, np.int64), (np.int32, np.int64), (np.int64, np.int32),
+    (np.float32, np.float32), (np.int32, np.float32), (np.float32, np.int32), (np.int64, np.float32),
+    (np.float32, np.int64), (np.float64, np.float64), (np.float32, np.float64), (np.float64, np.float32),
+    (np.int32, np.float64), (np.float64, np.int32), (np.int64, np.float64), (np.float64, np.int64),
+]
+
+
+@pytest.mark.parametrize("da,db", DTYPE_PAIRS, ids=[f"{np.dtype(a).name}-{np.dtype(b).name}" for a, b in DTYPE_PAIRS])
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div"])
+def test_binary_promotion(cuda_ok, oracle, op, da, db):
+    import ctorch_b200 as cb
+
+    if op == "div" and np.dtype(da).kind == "i" and np.dtype(db).kind == "i":
+        pytest.skip("integer division is refused")
+    rng = np.random.default_rng(11)
+    for layout in ("rows_long", "tiled", "general_offset", "flat_tail"):
+        sa, ra, sb, rb = BIN_LAYOUTS[layout]
+        a, ta = _pair(_rand(rng, sa, da), ra)
+        b, tb = _pair(_rand(rng, sb, db), rb)
+        got = getattr(cb, op)(ta, tb).cpu().numpy()
+        assert_bitexact(got, oracle.binary(op, a, b), f"{op} {layout}", nan_payload=False)
+
+
+@pytest.mark.parametrize("op", ["relu", "neg", "abs", "sqrt"])
+@pytest.mark.parametrize("dt", [np.float32, np.float64, np.int32, np.int64])
+def test_unary_exact(cuda_ok, oracle, op, dt):
+    import ctorch_b200 as cb
+
+    if op == "sqrt" and np.dtype(dt).kind == "i":
+        pytest.skip("float only")
+    rng = np.random.default_rng(5)
+    for shape, recipe in (((1_000_001,), []), ((256, 2048), [("permute", [1, 0])]), ((99, 77), [("slice", 1, 1, 77, 2)])):
+        base = _rand(rng, shape, dt)
+        if np.dtype(dt).kind == "f":
+            base.flat[::97] = np.nan
+            base.flat[1::89] = -0.0
+            if op == "sqrt":
+                base = np.abs(base)
+        x, tx = _pair(base, recipe)
+        got = getattr(cb, op)(tx).cpu().numpy()
+        assert_bitexact(got, oracle.unary(op, x), f"{op} {shape}", nan_payload=(op == "relu"))
+
+
+@pytest.mark.parametrize("op", ["exp", "log", "tanh", "sigmoid"])
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_unary_transcendental(cuda_ok, oracle, op, dt):
+    import ctorch_b200 as cb
+    from helpers import TOL_TRANSCENDENTAL
+
+    rng = np.random.default_rng(9)
+    base = (rng.standard_normal(300_001) * 4).astype(dt)
+    if op == "log":
+        base = np.abs(base) + np.asarray(1e-3, dt)
+    x, tx = _pair(base)
+    got = getattr(cb, op)(tx).cpu().numpy()
+    assert_close(got, oracle.unary(op, x), TOL_TRANSCENDENTAL[np.dtype(dt)], op)
+
+
+@pytest.mark.parametrize("op1,op2", [("sub", "mul"), ("mul", "add"), ("add", "div"), ("div", "sub")])
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_chain_is_bitwise_the_eager_pair(cuda_ok, oracle, op1, op2, dt):
+    import ctorch_b200 as cb
+
+    rng = np.random.default_rng(3)
+    for sx, sr in (((512, 8192), (1, 8192)), ((1000, 12), (1, 12)), ((77, 33), (33,))):
+        x, tx = _pair(_rand(rng, sx, dt))
+        r, tr = _pair(_rand(rng, sr, dt))
+        got = cb.binary_chain(op1, op2, tx, tr, tr).cpu().numpy()
+        ref = oracle.binary(op2, oracle.binary(op1, x, r), r)
+        assert_bitexact(got, ref, f"{op1}->{op2} {sx}", nan_payload=False)
+        eager = getattr(cb, op2)(getattr(cb, op1)(tx, tr), tr).cpu().numpy()
+        assert_bitexact(got, eager, "chain vs eager", nan_payload=False)
+
+
+RED_LAYOUTS = {
+    # name: (shape, recipe, dims, keepdim)
+    "inner_cta": ((96, 20_000), [], [1], True),
+    "inner_split": ((3, 1_000_003), [], [1], False),
+    "inner_warp": ((5000, 100), [], [1], False),
+    "inner_whole": ((2_000_003,), [], None, False),
+    "inner_offset_rows": ((300, 999), [("slice", 1, 1, 999, 1)], [1], False),
+    "outer": ((3000, 520), [], [0], False),
+    "outer_batched": ((3, 2000, 260), [], [1], True),
+    "outer_narrow": ((5000, 17), [], [0], False),
+    "outer_transposed": ((700, 900), [("permute", [1, 0])], [1], False),
+    "general_cta": ((1500, 1200), [("permute", [1, 0]), ("slice", 0, 0, 1200, 2)], None, False),
+    "general_thread": ((60, 7, 90), [], [0, 2], False),
+}
+
+
+def _red_dtypes(op):
+    if op == "mean":
+        return [np.float32, np.float64]
+    return [np.float32, np.float64, np.int32, np.int64, np.bool_]
+
+
+@pytest.mark.parametrize("layout", sorted(RED_LAYOUTS))
+@pytest.mark.parametrize("op", ["sum", "mean", "prod", "max", "min"])
+def test_reduction_layouts(cuda_ok, oracle, op, layout):
+    import ctorch_b200 as cb
+
+    shape, recipe, dims, kd = RED_LAYOUTS[layout]
+    rng = np.random.default_rng(_seed(op, layout))
+    for dt in _red_dtypes(op):
+        base = _rand(rng, shape, dt)
+        if op == "prod" and np.dtype(dt).kind == "f":
+            base = (1 + 1e-4 * base).astype(dt)
+        if op in ("max", "min") and np.dtype(dt).kind == "f":
+            base.flat[::1013] = np.nan
+            base.flat[7::501] = -0.0
+            base.flat[9::503] = 0.0
+        x, tx = _pair(base, recipe)
+        got = getattr(cb, op)(tx, dims, kd).cpu().numpy()
+        ref = oracle.reduce(op, x, dims, kd)
+        what = f"{op} {layout} {np.dtype(dt).name}"
+        if op in ("sum", "mean", "prod") and np.dtype(dt).kind == "f":
+            assert_close(got, ref, TOL_SUM[np.dtype(dt)], what)
+        else:
+            assert_bitexact(got, ref, what)
+
+
+IDX_LAYOUTS = {
+    # name: (shape, recipe, dim)
+    "outer_cols": ((4000, 1000), [], 0),
+    "outer_batched": ((3, 1500, 130), [], 1),
+    "outer_narrow": ((3000, 9), [], 0),
+    "inner_rows": ((3000, 1000), [], 1),
+    "inner_long": ((4, 1_000_000), [], 1),
+    "general": ((90, 80, 70), [("permute", [2, 0, 1])], 2),
+}
+
+
+@pytest.mark.parametrize("layout", sorted(IDX_LAYOUTS))
+@pytest.mark.parametrize("op", ["max", "min"])
+@pytest.mark.parametrize("dt", [np.float32, np.float64, np.int32, np.int64, np.bool_])
+def test_reduce_index_layouts(cuda_ok, oracle, op, layout, dt):
+    import ctorch_b200 as cb
+
+    shape, recipe, dim = IDX_LAYOUTS[layout]
+    rng = np.random.default_rng(_seed(op, layout, np.dtype(dt).name))
+    base = _rand(rng, shape, dt)
+    if np.dtype(dt).kind == "i":
+        base = (base % 7).astype(dt)  # many ties -> first index must win
+    if np.dtype(dt).kind == "f":
+        base = np.round(base * 4) / 4  # ties
+        base = base.astype(dt)
+        base.flat[::4099] = np.nan
+        base.flat[5::307] = -0.0
+    x, tx = _pair(base, recipe)
+    v, i = getattr(cb, op)(tx, dim, False)
+    rv, ri = oracle.reduce_idx(op, x, dim, False)
+    assert_bitexact(v.cpu().numpy(), rv, f"{op} values {layout}")
+    assert_bitexact(i.cpu().numpy(), ri, f"{op} indices {layout}")
+    a = getattr(cb, "arg" + op)(tx, dim, True).cpu().numpy()
+    assert_bitexact(a, oracle.reduce_idx(op, x, dim, True, values=False), f"arg{op} {layout}")
+
+
+def test_reductions_are_deterministic(cuda_ok):
+    import torch
+
+    import ctorch_b200 as cb
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(3, 5_000_000, device="cuda", generator=g)
+    a = cb.sum(x, [1])
+    b = cb.sum(x, [1])
+    assert torch.equal(a, b)
+    y = torch.randn(4096, 4096, device="cuda", generator=g)
+    assert torch.equal(cb.max(y, 0, False).indices, cb.max(y, 0, False).indices)
+    assert torch.equal(cb.sum(y), cb.sum(y))
+
+
+GATHER = {
+    # name: (src shape, src recipe, dim, n_idx, idx dtype)
+    "rows_1k": ((5000, 256), [], 0, 20000, np.int64),
+    "rows_i32": ((5000, 256), [], 0, 7000, np.int32),
+    "rows_odd_bytes": ((3000, 3), [], 0, 9000, np.int64),
+    "inner_dim": ((40, 300, 16), [], 1, 500, np.int64),
+    "last_dim": ((200, 300), [], 1, 1000, np.int64),
+    "strided_src": ((300, 400), [("permute", [1, 0])], 0, 2000, np.int64),
+    "sliced_src": ((400, 300), [("slice", 1, 10, 300, 1)], 0, 2000, np.int32),
+}
+
+
+@pytest.mark.parametrize("layout", sorted(GATHER))
+@pytest.mark.parametrize("dt", [np.float32, np.float64, np.int32, np.bool_])
+def test_index_select_layouts(cuda_ok, oracle, layout, dt):
+    import torch
+
+    import ctorch_b200 as cb
+
+    shape, recipe, dim, n, idt = GATHER[layout]
+    rng = np.random.default_rng(_seed(layout, np.dtype(dt).name))
+    x, tx = _pair(_rand(rng, shape, dt), recipe)
+    size = x.shape[dim]
+    idx = rng.integers(-size, size, n).astype(idt)
+    ti = torch.from_numpy(idx).cuda()
+    got = cb.index_select(tx, dim, ti).cpu().numpy()
+    assert_bitexact(got, oracle.index_select(x, dim, idx), layout)
+    # strided index vector
+    got2 = cb.index_select(tx, dim, ti[::3]).cpu().numpy()
+    assert_bitexact(got2, oracle.index_select(x, dim, idx[::3]), layout + " strided idx")
+
+
+def test_index_select_error_writes_nothing(cuda_ok):
+    import torch
+
+    import ctorch_b200 as cb
+
+    src = torch.randn(100, 64, device="cuda")
+    idx = torch.tensor([1, 2, 100, 3], device="cuda")
+    out, status = cb.index_select_async(src, 0, idx)
+    sentinel = torch.full_like(out, 7.0)
+    out.copy_(sentinel)
+    out2, status2 = cb.index_select_async(src, 0, idx)
+    torch.cuda.synchronize()
+    assert int(status2[:4].view(torch.int32)[0].item()) == 1
+    assert int(status2[8:16].view(torch.int64)[0].item()) == 100
+    with pytest.raises(cb.ShapeError):
+        cb.index_select(src, 0, torch.tensor([-101], device="cuda"))
+    with pytest.raises(cb.ShapeError):
+        cb.index_select(src, 0, torch.tensor([-(2**63)], device="cuda"))
+    # a valid call after an error on the same stream still works
+    ok = cb.index_select(src, 0, torch.tensor([99, -100], device="cuda"))
+    assert torch.equal(ok, src[[99, 0]])
+
+
+def test_front_door_errors(cuda_ok):
+    import torch
+
+    import ctorch_b200 as cb
+
+    a = torch.ones(3, 4, device="cuda")
+    with pytest.raises(cb.DTypeError):
+        cb.add(a.bool(), a)
+    with pytest.raises(cb.DTypeError):
+        cb.div(a.int(), a.int())
+    with pytest.raises(cb.ShapeError):
+        cb.add(a, torch.ones(5, device="cuda"))
+    with pytest.raises(cb.DeviceError):
+        cb.add(a, torch.ones(3, 4))
+    with pytest.raises(cb.DTypeError):
+        cb.add_(a.int(), a)  # in-place dtype must already be the promoted dtype
+    with pytest.raises(cb.AliasError):
+        cb.add_(a[:, 1:], a[:, :3])
+    with pytest.raises(cb.ShapeError):
+        cb.max(torch.ones(3, 0, device="cuda"), [1])
+    with pytest.raises(cb.ShapeError):
+        cb.argmax(torch.ones(3, 0, device="cuda"), 1)
+    with pytest.raises(cb.ShapeError):
+        cb.sum(a, [0, -2])
+    with pytest.raises(cb.DTypeError):
+        cb.mean(a.int())
+    assert cb.sum(torch.ones(3, 0, device="cuda"), [1]).tolist() == [0.0, 0.0, 0.0]
+    assert torch.isnan(cb.mean(torch.ones(3, 0, device="cuda"), [1])).all()
