@@ -1,0 +1,455 @@
+#!/usr/bin/env python3
+"""Benchmark of the row-sharded eager-op workload on 1..8 B200s (one process per GPU).
+
+Workload (the multi-GPU configuration of the hot path): X float32 [262144, 8192] ~ N(0, 1)
+(seed 4), rows split into contiguous blocks across the ranks, and r float32 [1, 8192] ~ U(-1, 1)
+(seed 4, stream 1) on every rank. One step:
+    Y = (X - r) * r          fused into one pass, bit-identical to ctorch's sub then mul
+    s = sum(Y)               float64 partial per rank, NCCL all-gather, rank-order combine
+    k = argmin(Y, dim=1)     per row, first index on ties
+Total work is fixed as GPUs are added (strong scaling). `value` is elements of X processed per
+second by the whole job, device-timed with CUDA events, max over ranks. Inputs (8 GiB in total)
+are larger than the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+--impl reference times ctorch's own CPU implementation of the same step (its public front-doors,
+compiled from its sources into oracle/_ref/) on a bounded row sample, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+ROWS, COLS = 262144, 8192
+SEED = 4
+METRIC = "HBM GB/s per op vs ~8 TB/s peak; elements/sec at 1/2/4/8 B200 vs ctorch CPU"
+UNIT = "elements/s"
+WORKLOAD = ("row-sharded Y=(X-r)*r, sum(Y), argmin(Y,1); X f32[262144,8192] ~N(0,1) seed 4, "
+            "r f32[1,8192] ~U(-1,1)")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def base_config(world):
+    return {"workload": WORKLOAD, "rows": ROWS, "cols": COLS, "parallelism": f"rows{world}",
+            "l2": "inputs larger than L2 (no flush)", "data": "synthetic, seeded splitmix64"}
+
+
+# ------------------------------------------------------------------------------- CPU (ctorch)
+
+def host_inputs(rows):
+    from ctorch_b200.synth import NORMAL, UNIFORM, host_fill
+
+    x = host_fill((rows, COLS), "float32", NORMAL, SEED, 0, 0.0, 1.0)
+    r = host_fill((1, COLS), "float32", UNIFORM, SEED, 1, -1.0, 1.0)
+    return x, r
+
+
+def ctorch_cpu_step(ref, x, r):
+    """ctorch's public CPU front-doors: sub, mul (src/ops/binary_ops_cpu.cpp:251-254), sum
+    (reduction_ops_cpu.cpp:463), argmin (:497)."""
+    t = ref.binary("sub", x, r)
+    y = ref.binary("mul", t, r)
+    s = ref.reduce("sum", y)
+    k = ref.arg("argmin", y, 1)
+    return s, k
+
+
+def time_ctorch_cpu(rows, steps, warmup):
+    from oracle.oracle import ref as get_ref
+
+    ref = get_ref()
+    xh, rh = host_inputs(rows)
+    x, r = ref.tensor(xh), ref.tensor(rh)
+    for _ in range(warmup):
+        ctorch_cpu_step(ref, x, r)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        ctorch_cpu_step(ref, x, r)
+        ts.append(time.perf_counter() - t0)
+    per_step = statistics.mean(ts)
+    return rows * COLS / per_step, per_step
+
+
+def calibrate_rows(budget_s, n_steps, probe_rows=1024):
+    """Rows per CPU step so that n_steps fit in budget_s (powers of two, 512..65536)."""
+    _, t = time_ctorch_cpu(probe_rows, 1, 0)
+    per_row = t / probe_rows
+    rows = max(512, min(65536, int(budget_s / max(1, n_steps) / per_row)))
+    p = 512
+    while p * 2 <= rows:
+        p *= 2
+    return p
+
+
+def run_reference(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    rows = args.cpu_rows or calibrate_rows(150.0, args.steps + args.warmup)
+    value, per_step = time_ctorch_cpu(rows, args.steps, args.warmup)
+    sample = (f"{rows} of {ROWS} rows per step ({rows * COLS} elements), ctorch front-doors "
+              f"sub, mul, sum, argmin on CPU tensors, 1 thread (ctorch's CPU path is single-threaded)")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": base_config(world), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            cmd += ["-i", vis]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in csv.reader(io.StringIO(out)):
+            if len(row) < 9:
+                continue
+            try:
+                sm.append(float(row[1]))
+                smax.append(float(row[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, row[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic_per_row():
+    """DRAM bytes (read + write) per row of X for the fused elementwise kernel, from the committed
+    ncu summary (profiles/ncu_traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["chain_bytes"]) / float(d["chain_rows"])
+    except (OSError, KeyError, ValueError, ZeroDivisionError):
+        return None
+
+
+# ------------------------------------------------------------------------------- GPU arm
+
+def run_b200(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ctorch_b200 as cb
+    from ctorch_b200.sharded import ShardedSum, row_shard, sharded_step
+    from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
+
+    rank, world, local = env_rank()
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    shard = row_shard(ROWS, rank, world)
+    x = torch.empty((shard.rows, COLS), dtype=torch.float32, device=dev)
+    r = torch.empty((1, COLS), dtype=torch.float32, device=dev)
+    device_fill(x, NORMAL, SEED, 0, 0.0, 1.0, first=shard.start * COLS)
+    device_fill(r, UNIFORM, SEED, 1, -1.0, 1.0)
+    summer = ShardedSum(dev, world)
+    torch.cuda.synchronize()
+
+    def step():
+        return sharded_step(x, r, summer)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    cb.launch_count_reset()
+    start.record()
+    for i in range(K):
+        ev[i][0].record()
+        y = cb.binary_chain("sub", "mul", x, r, r)
+        ev[i][1].record()
+        summer(y)
+        ev[i][2].record()
+        cb.argmin(y, 1)
+        ev[i][3].record()
+        del y
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = cb.launch_count()
+    clocks = sampler.stop() if rank == 0 else None
+    elapsed = max_over_ranks(start.elapsed_time(end))
+    chain_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    sum_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    arg_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
+    chain_ms = max_over_ranks(chain_ms)
+    sum_ms = max_over_ranks(sum_ms)
+    arg_ms = max_over_ranks(arg_ms)
+    total_launches = int(sum_over_ranks(launches))
+
+    # eager drop-in sequence (sub then mul as two kernels) for comparison
+    eager_steps = min(K, 20)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(eager_steps):
+        y = cb.mul(cb.sub(x, r), r)
+        summer(y)
+        cb.argmin(y, 1)
+        del y
+    e1.record()
+    torch.cuda.synchronize()
+    eager_ms = max_over_ranks(e0.elapsed_time(e1)) / eager_steps
+
+    # end to end: pinned host input -> device, step, device -> pinned host results
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.empty((shard.rows, COLS), dtype=torch.float32, pin_memory=True)
+        xh.copy_(x)
+        rh = torch.empty((1, COLS), dtype=torch.float32, pin_memory=True)
+        rh.copy_(r)
+        kh = torch.empty((shard.rows,), dtype=torch.int64, pin_memory=True)
+        sh = torch.empty((), dtype=torch.float32, pin_memory=True)
+        xd = torch.empty_like(x)
+        rd = torch.empty_like(r)
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            rd.copy_(rh, non_blocking=True)
+            y, s, k = sharded_step(xd, rd, summer)
+            sh.copy_(s, non_blocking=True)
+            kh.copy_(k, non_blocking=True)
+
+        e2e_steps = max(2, min(K, 5))
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        a1.record()
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(a0.elapsed_time(a1)) / e2e_steps
+        e2e = {"value": ROWS * COLS / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": ROWS * COLS * 4 + world * COLS * 4,
+               "d2h_bytes_per_step": ROWS * 8 + world * 4, "ms_per_step": e2e_ms,
+               "path": "pinned host X, r -> HBM; fused chain, sharded sum, argmin through the C ABI; "
+                       "s and k -> pinned host"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = args.cpu_rows or 32768
+        v, per_step = time_ctorch_cpu(rows, 2, 1)
+        cpu = {"value": v, "unit": UNIT, "cores": 1, "kind": "reference",
+               "sample": f"{rows} of {ROWS} rows ({rows * COLS} elements) through ctorch's CPU "
+                         f"front-doors sub, mul, sum, argmin; mean of 2 steps after 1 warm-up, "
+                         f"{per_step:.2f} s per step"}
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        chain_bytes = shard.rows * COLS * 4 * 2 + COLS * 4
+        achieved = chain_bytes / (chain_ms / 1e3) / 1e9
+        tpr = ncu_traffic_per_row()
+        ms_per_step = elapsed / K
+        line = {
+            "metric": METRIC,
+            "value": ROWS * COLS * K / (elapsed / 1e3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": K,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": base_config(world),
+            "gbs": ROWS * COLS * 4 * 4 / (ms_per_step / 1e3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "kernel": "fused (X - r) * r (ew_rows_long, FnChain)",
+                         "algorithmic_bytes": chain_bytes,
+                         "traffic": tpr * shard.rows if tpr else None},
+            "kernels_ms": {"chain": chain_ms, "sum_allgather_combine": sum_ms, "argmin": arg_ms},
+            "eager_ms_per_step": eager_ms,
+            "gpu_launches": total_launches,
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del summer
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ------------------------------------------------------------------------------- profiling cases
+
+def run_case(args):
+    """Launches one kernel of the hot path a few times on a reduced input, for an ncu capture
+    (e.g. `ncu --set full -k regex:ew_rows -c 3 python bench.py --case chain --rows 16384`).
+    Inputs stay larger than L2 at the default sizes. Prints nothing to time."""
+    import torch
+
+    import ctorch_b200 as cb
+    from ctorch_b200.sharded import ShardedSum
+    from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
+
+    dev = torch.device("cuda", 0)
+    rows = args.rows
+    t = lambda shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
+    case = args.case
+    if case in ("chain", "sum", "argmin", "sub"):
+        x = device_fill(t((rows, COLS)), NORMAL, SEED, 0, 0.0, 1.0)
+        r = device_fill(t((1, COLS)), UNIFORM, SEED, 1, -1.0, 1.0)
+        y = cb.binary_chain("sub", "mul", x, r, r)
+        summer = ShardedSum(dev, 1)
+        fn = {"chain": lambda: cb.binary_chain("sub", "mul", x, r, r), "sub": lambda: cb.sub(x, r),
+              "sum": lambda: summer(y), "argmin": lambda: cb.argmin(y, 1)}[case]
+    elif case in ("add", "relu"):
+        a = device_fill(t((4096, 4096)), UNIFORM, 0, 0, -1.0, 1.0)
+        b = device_fill(t((1, 4096)), UNIFORM, 0, 1, -1.0, 1.0)
+        fn = (lambda: cb.add(a, b)) if case == "add" else (lambda: cb.relu(a))
+    elif case in ("sum_rows", "argmax_cols", "max_cols", "prod_rows"):
+        x = device_fill(t((8192, 8192)), NORMAL, 1, 0, 0.0, 1.0)
+        fn = {"sum_rows": lambda: cb.sum(x, [1], True), "prod_rows": lambda: cb.prod(x, [1]),
+              "argmax_cols": lambda: cb.argmax(x, 0), "max_cols": lambda: cb.max(x, 0)}[case]
+    elif case == "index_select":
+        tab = device_fill(t((1_000_000, 256)), NORMAL, 2, 0, 0.0, 1.0)
+        idx = device_fill(t((rows * 16,), torch.int64), UNIFORM, 2, 2, 0, 999_999)
+        fn = lambda: cb.index_select_async(tab, 0, idx)  # noqa: E731
+    elif case in ("mul_t", "div_b"):
+        i = device_fill(t((64, 512, 1024), torch.int32), UNIFORM, 3, 0, -1000, 1000)
+        f = device_fill(t((64, 1024, 512)), UNIFORM, 3, 1, -1.0, 1.0)
+        d = device_fill(t((1, 512, 1), torch.float64), UNIFORM, 3, 2, 0.5, 2.0)
+        p = cb.mul(i, f.permute(0, 2, 1))
+        fn = (lambda: cb.mul(i, f.permute(0, 2, 1))) if case == "mul_t" else (lambda: cb.div(p, d))
+    else:
+        raise SystemExit(f"unknown case {case}")
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-rows", type=int, default=0, help="rows per CPU step (0 = auto)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--case", default=None,
+                    help="profiling mode: launch one kernel (chain, sub, sum, argmin, add, relu, sum_rows, "
+                         "prod_rows, argmax_cols, max_cols, index_select, mul_t, div_b) --warmup + --steps times")
+    ap.add_argument("--rows", type=int, default=16384, help="rows of X for --case (default 16384: 512 MiB)")
+    args = ap.parse_args()
+    if args.case:
+        return run_case(args)
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -4,8 +4,10 @@
 #include <atomic>
 #include <cstdio>
 #include <exception>
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 
 #include "common.cuh"
 #include "plan.cuh"
@@ -64,6 +66,27 @@ int sm_count() {
         cache[dev] = n;
     }
     return cache[dev];
+}
+
+int resident_ctas(const void* fn, int block, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, int, size_t>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 4;
+    }
+    const auto key = std::make_tuple(fn, dev, block, smem);
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, block, smem) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = 1;
+    }
+    cache[key] = n;
+    return n;
 }
 
 size_t dtype_size(int dt) {

@@ -21,6 +21,9 @@ int fail(int status, const std::string& msg);         // records msg for ctb_las
 int check_launch(const char* what);                   // cudaGetLastError -> CTB_ERR_CUDA
 void count_launch(int n = 1);                         // feeds ctb_launch_count
 int sm_count();                                       // SMs of the current device (cached)
+// Resident CTAs per SM for `fn` at this block size / dynamic smem on the current device (cached;
+// 4 when no device is present, e.g. when planning on a host without a GPU).
+int resident_ctas(const void* fn, int block, size_t smem = 0);
 size_t dtype_size(int dt);
 int promote(int a, int b);                            // -1 for unsupported
 const char* dtype_name(int dt);

@@ -168,15 +168,72 @@ __global__ void __launch_bounds__(kEwBlock) ew_rows_long(EwArgs p, Fn fn) {
 
 template <class Fn, class O, class I0, class I1, class I2, int NIN>
 __global__ void __launch_bounds__(kEwBlock) ew_rows_short(EwArgs p, Fn fn) {
+    constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
+    constexpr int U = kEwUnroll;
+    const int r = p.rank - 1;
+    const bool b0 = p.stride[1][r] == 0;
+    const bool b1 = NIN > 1 && p.stride[2][r] == 0;
+    const bool b2 = NIN > 2 && p.stride[3][r] == 0;
+    O* __restrict__ out = static_cast<O*>(p.out);
+    const I0* __restrict__ in0 = static_cast<const I0*>(p.in[0]);
+    const I1* __restrict__ in1 = static_cast<const I1*>(p.in[1]);
+    const I2* __restrict__ in2 = static_cast<const I2*>(p.in[2]);
     const int64_t nvec = p.rows * p.vpr;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t v = tid; v < nvec; v += nthr) {
-        uint64_t row, c;
-        p.aux.divmod(static_cast<uint64_t>(v), row, c);
-        int64_t off[kMaxOps];
-        ew_decode_row(p, row, NIN + 1, off);
-        ew_row_segment<Fn, O, I0, I1, I2, NIN>(p, fn, off, static_cast<int64_t>(c), 0, 1);
+    for (int64_t base = tid; base < nvec; base += nthr * U) {
+        int64_t oo[U];
+        Pack<I0, V> x0[U];
+        Pack<I1, V> x1[U];
+        Pack<I2, V> x2[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t v = base + u * nthr;
+            oo[u] = -1;
+            if (v < nvec) {
+                uint64_t row, c;
+                p.aux.divmod(static_cast<uint64_t>(v), row, c);
+                int64_t off[kMaxOps];
+                ew_decode_row(p, row, NIN + 1, off);
+                const int64_t cv = static_cast<int64_t>(c) * V;
+                oo[u] = off[0] + cv;
+                if (b0) {
+                    const I0 s = in0[off[1]];
+#pragma unroll
+                    for (int e = 0; e < V; ++e) x0[u].v[e] = s;
+                } else {
+                    x0[u] = load_pack<I0, V>(in0 + off[1] + cv);
+                }
+                if constexpr (NIN > 1) {
+                    if (b1) {
+                        const I1 s = in1[off[2]];
+#pragma unroll
+                        for (int e = 0; e < V; ++e) x1[u].v[e] = s;
+                    } else {
+                        x1[u] = load_pack<I1, V>(in1 + off[2] + cv);
+                    }
+                }
+                if constexpr (NIN > 2) {
+                    if (b2) {
+                        const I2 s = in2[off[3]];
+#pragma unroll
+                        for (int e = 0; e < V; ++e) x2[u].v[e] = s;
+                    } else {
+                        x2[u] = load_pack<I2, V>(in2 + off[3] + cv);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (oo[u] >= 0) {
+                Pack<O, V> o;
+#pragma unroll
+                for (int e = 0; e < V; ++e)
+                    o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, x0[u].v[e], x1[u].v[e], x2[u].v[e]);
+                store_pack<O, V>(out + oo[u], o);
+            }
+        }
     }
 }
 
@@ -244,21 +301,41 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled(EwArgs p, Fn fn) {
         }
         const int64_t l0 = static_cast<int64_t>(tl) * kTile;
         const int64_t p0 = static_cast<int64_t>(tp) * kTile;
-        for (int k = threadIdx.x; k < kTile * kTile; k += kEwBlock) {
+        constexpr int kPer = kTile * kTile / kEwBlock;
+        // issue every global load of the tile (transposed input and the row-major operand) before
+        // the barrier, so both latencies overlap
+        X xr[kPer];
+        Y yr[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int k = threadIdx.x + j * kEwBlock;
             const int li = k >> 6, pi = k & 63;
             const int64_t pp = p0 + pi, ll = l0 + li;
-            if (pp < P && ll < L) tile[li][pi] = xin[offX + pp + ll * sXl];
+            if (pp < P && ll < L) xr[j] = xin[offX + pp + ll * sXl];
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int k = threadIdx.x + j * kEwBlock;
+            const int pi = k >> 6, li = k & 63;
+            const int64_t pp = p0 + pi, ll = l0 + li;
+            if (pp < P && ll < L) yr[j] = yin[offY + pp * sYp + ll * sYl];
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int k = threadIdx.x + j * kEwBlock;
+            tile[k >> 6][k & 63] = xr[j];
         }
         __syncthreads();
-        for (int k = threadIdx.x; k < kTile * kTile; k += kEwBlock) {
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int k = threadIdx.x + j * kEwBlock;
             const int pi = k >> 6, li = k & 63;
             const int64_t pp = p0 + pi, ll = l0 + li;
             if (pp < P && ll < L) {
                 const X x = tile[li][pi];
-                const Y y = yin[offY + pp * sYp + ll * sYl];
                 O o;
-                if constexpr (XOP == 1) o = fn(x, y);
-                else o = fn(y, x);
+                if constexpr (XOP == 1) o = fn(x, yr[j]);
+                else o = fn(yr[j], x);
                 out[offO + pp * sOp + ll] = o;
             }
         }
@@ -288,7 +365,7 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
     }
     case EwPath::RowsShort: {
         const int64_t nvec = a.rows * a.vpr;
-        ew_rows_short<Fn, O, I0, I1, I2, NIN><<<grid_for((nvec + kEwBlock - 1) / kEwBlock, 16), kEwBlock, 0, st>>>(a, fn);
+        ew_rows_short<Fn, O, I0, I1, I2, NIN><<<grid_for((nvec + kEwBlock * kEwUnroll - 1) / (kEwBlock * kEwUnroll), 16), kEwBlock, 0, st>>>(a, fn);
         break;
     }
     case EwPath::Tiled: {

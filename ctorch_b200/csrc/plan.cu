@@ -177,7 +177,7 @@ int plan_elementwise(const ctb_view* out, const ctb_view* const* ins, int nin, c
     if (inner_ok && aligned && a.L % vec == 0) {
         a.vpr = a.L / vec;
         constexpr int kBlock = 256, kUnroll = 4;
-        if (a.vpr >= 128) {
+        if (a.vpr >= kBlock * kUnroll) {
             const int64_t seg = static_cast<int64_t>(kBlock) * kUnroll;
             a.aux = FastDiv(static_cast<uint64_t>((a.vpr + seg - 1) / seg));
             plan.path = EwPath::RowsLong;
@@ -352,9 +352,10 @@ int plan_reduction(const ctb_view* in, const ctb_view* out, const ctb_view* out2
     return CTB_OK;
 }
 
-size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int outer_vec) {
+size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int outer_vec,
+                             const RedOcc& occ) {
     RedArgs& a = plan.args;
-    const int64_t target = static_cast<int64_t>(sm_count()) * 8;  // resident 256-thread CTAs
+    const int64_t sms = sm_count();
     plan.block = 256;
     a.split = 1;
     a.chunk = a.red;
@@ -365,19 +366,21 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
         break;
     case RedPath::Inner: {
         const int64_t K = a.K;
-        if (K < 2048 && a.kept >= 64) {
-            // one warp per row
+        if (K <= 65536 && a.kept >= sms * 16) {
+            // one warp per row, persistent grid of one wave
             plan.warp_rows = true;
-            const int64_t warps = a.kept;
-            plan.grid = grid_for((warps + 7) / 8, 32);
+            const int64_t ctas = (a.kept + 7) / 8;
+            const int64_t slots = sms * occ.inner_warp;
+            plan.grid = static_cast<unsigned>(ctas < slots ? ctas : slots);
             break;
         }
         plan.warp_rows = false;
+        const int64_t slots = sms * occ.inner_cta;
         int64_t split = 1;
-        if (a.kept < target) {
-            split = (target + a.kept - 1) / a.kept;
-            const int64_t max_split = std::max<int64_t>(1, K / 4096);
-            split = std::min(split, max_split);
+        if (a.kept < slots) {
+            split = slots / a.kept;
+            split = std::min<int64_t>(split, std::max<int64_t>(1, K / 4096));
+            split = std::max<int64_t>(split, 1);
         }
         // chunks are whole 64-byte multiples so every split starts 16-byte aligned when the row does
         int64_t chunk = (K + split - 1) / split;
@@ -387,7 +390,8 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
         a.split = static_cast<int>(split);
         a.chunk = chunk;
         a.aux = FastDiv(static_cast<uint64_t>(split));
-        plan.grid = grid_for(a.kept * split, 32);
+        const int64_t work = a.kept * split;
+        plan.grid = static_cast<unsigned>(work < slots ? work : slots);
         if (split > 1) scratch = static_cast<size_t>(a.kept * split) * state_bytes;
         break;
     }
@@ -396,10 +400,12 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
         const int64_t tiles_n = (a.N + plan.col_tile - 1) / plan.col_tile;
         const int64_t batch = a.kept / a.N;
         const int64_t tiles = tiles_n * batch;
+        const int64_t slots = sms * occ.outer;
         int64_t split = 1;
-        if (tiles < target) {
-            split = (target + tiles - 1) / tiles;
+        if (tiles < slots) {
+            split = slots / tiles;
             split = std::min<int64_t>(split, std::max<int64_t>(1, a.K / 64));
+            split = std::max<int64_t>(split, 1);
         }
         int64_t chunk = (a.K + split - 1) / split;
         split = (a.K + chunk - 1) / chunk;
@@ -407,14 +413,16 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
         a.chunk = chunk;
         a.aux = FastDiv(static_cast<uint64_t>(tiles_n));
         a.aux2 = FastDiv(static_cast<uint64_t>(split));
-        plan.grid = grid_for(tiles * split, 64);
+        const int64_t work = tiles * split;
+        plan.grid = static_cast<unsigned>(work < slots ? work : slots);
         if (split > 1) scratch = static_cast<size_t>(a.kept * split) * state_bytes;
         break;
     }
     case RedPath::General: {
+        const int64_t slots = sms * occ.general_cta;
         // few outputs with long reduced ranges: CTAs share an output; otherwise one thread each
-        if (a.kept < target * 32 && a.red >= 1024) {
-            int64_t split = std::max<int64_t>(1, target / a.kept);
+        if (a.kept < slots * 32 && a.red >= 1024) {
+            int64_t split = std::max<int64_t>(1, slots / a.kept);
             split = std::min<int64_t>(split, std::max<int64_t>(1, a.red / 4096));
             const int64_t chunk = (a.red + split - 1) / split;
             split = (a.red + chunk - 1) / chunk;
@@ -422,7 +430,8 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
             a.chunk = chunk;
             a.aux = FastDiv(static_cast<uint64_t>(split));
             plan.warp_rows = false;
-            plan.grid = grid_for(a.kept * split, 32);
+            const int64_t work = a.kept * split;
+            plan.grid = static_cast<unsigned>(work < slots ? work : slots);
             if (split > 1) scratch = static_cast<size_t>(a.kept * split) * state_bytes;
         } else {
             plan.warp_rows = true;  // here: one thread per output

@@ -119,10 +119,17 @@ struct RedPlan {
 int plan_reduction(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint32_t mask,
                    RedPlan& plan);
 
+// Resident 256-thread CTAs per SM of each reduction kernel (register-limited, so it differs per
+// reducer); grids are sized to whole waves of these.
+struct RedOcc {
+    int inner_cta = 4, inner_warp = 4, outer = 4, general_cta = 4;
+};
+
 // Chooses split counts / grid for a planned reduction. `state_bytes` is the size of one partial
 // state, `outer_vec` the column-strip pack width the Outer kernel will use; returns the scratch
 // bytes the plan needs.
-size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int outer_vec);
+size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int outer_vec,
+                             const RedOcc& occ);
 
 const char* red_path_name(RedPath p);
 

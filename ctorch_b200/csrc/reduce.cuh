@@ -412,6 +412,9 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize(Red
 // ------------------------------------------------------------------------------------------------
 // launcher
 
+// Outer-path vector width for element type T.
+template <class T> constexpr int outer_vec() { return sizeof(T) >= 8 ? 2 : 4; }
+
 template <class R>
 int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t need,
                      cudaStream_t st) {
@@ -431,7 +434,7 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
         break;
     case RedPath::Outer: {
         using T = typename R::In;
-        constexpr int VMAX = sizeof(T) >= 8 ? 2 : 4;
+        constexpr int VMAX = outer_vec<T>();
         if (plan.col_tile == 32 * VMAX) red_outer<R, VMAX><<<plan.grid, kRedBlock, 0, st>>>(a);
         else red_outer<R, 1><<<plan.grid, kRedBlock, 0, st>>>(a);
         break;
@@ -450,9 +453,6 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
     count_launch(launches);
     return check_launch("reduction");
 }
-
-// Outer-path vector width the kernels use for element type T (see launch_reduction).
-template <class T> constexpr int outer_vec() { return sizeof(T) >= 8 ? 2 : 4; }
 
 // Whether the Outer strip kernel may use V-wide loads for this plan.
 inline bool outer_vec_ok(const RedPlan& plan, int elem_bytes, int V) {
@@ -475,7 +475,13 @@ int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint
     if (rc) return rc;
     constexpr int V = outer_vec<T>();
     const bool vec_ok = outer_vec_ok(plan, sizeof(T), V);
-    need = finish_reduction_plan(plan, sizeof(T), sizeof(typename R::State), vec_ok ? V : 1);
+    RedOcc occ;
+    occ.inner_cta = resident_ctas(reinterpret_cast<const void*>(&red_inner_cta<R>), kRedBlock);
+    occ.inner_warp = resident_ctas(reinterpret_cast<const void*>(&red_inner_warp<R>), kRedBlock);
+    occ.outer = vec_ok ? resident_ctas(reinterpret_cast<const void*>(&red_outer<R, V>), kRedBlock)
+                       : resident_ctas(reinterpret_cast<const void*>(&red_outer<R, 1>), kRedBlock);
+    occ.general_cta = resident_ctas(reinterpret_cast<const void*>(&red_general_cta<R>), kRedBlock);
+    need = finish_reduction_plan(plan, sizeof(T), sizeof(typename R::State), vec_ok ? V : 1, occ);
     return CTB_OK;
 }
 

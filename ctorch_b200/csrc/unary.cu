@@ -10,10 +10,20 @@ namespace ctb {
 template <int OP, class T> struct FnUnary {
     __device__ __forceinline__ T operator()(T x) const {
         if constexpr (OP == CTB_RELU) {
-            if constexpr (is_float_v<T>) {
-                if (x != x) return x;
+            // Selected on the bit pattern so a NaN comes back with its own bits (a float max or
+            // compare-select may hand back a canonical NaN instead): positive values and NaNs pass,
+            // everything else (including -0.0) becomes +0.0.
+            if constexpr (std::is_same_v<T, float>) {
+                const uint32_t b = __float_as_uint(x);
+                const bool nan = (b & 0x7fffffffu) > 0x7f800000u;
+                return __uint_as_float((static_cast<int32_t>(b) > 0 || nan) ? b : 0u);
+            } else if constexpr (std::is_same_v<T, double>) {
+                const uint64_t b = static_cast<uint64_t>(__double_as_longlong(x));
+                const bool nan = (b & 0x7fffffffffffffffULL) > 0x7ff0000000000000ULL;
+                return __longlong_as_double(static_cast<long long>((static_cast<int64_t>(b) > 0 || nan) ? b : 0ull));
+            } else {
+                return x > T(0) ? x : T(0);
             }
-            return x > T(0) ? x : T(0);
         } else if constexpr (OP == CTB_NEG) {
             if constexpr (is_float_v<T>) return -x;
             else return static_cast<T>(std::make_unsigned_t<T>(0) - static_cast<std::make_unsigned_t<T>>(x));

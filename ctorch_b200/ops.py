@@ -10,7 +10,7 @@ CPU tensors raise DeviceError.
 """
 from __future__ import annotations
 
-import ctypes
+import builtins as _bi
 from collections import namedtuple
 from typing import Sequence
 
@@ -28,7 +28,7 @@ def promote_types(a: torch.dtype, b: torch.dtype) -> torch.dtype:
     """ctorch's lattice bool < int32 < int64 < float32 < float64 (src/type_promotion.cpp:45-62)."""
     if a not in _PROMOTION_ORDER or b not in _PROMOTION_ORDER:
         raise DTypeError("ctorch::promote_types: bfloat16 not supported")
-    return max(a, b, key=_PROMOTION_ORDER.index)
+    return _bi.max(a, b, key=_PROMOTION_ORDER.index)
 
 
 def _raise(status: int, name: str):
@@ -64,7 +64,7 @@ def _cuda(name: str, *ts: torch.Tensor):
 
 def broadcast_shape(sa: Sequence[int], sb: Sequence[int]) -> tuple:
     """Right-aligned broadcast (src/ops/broadcast.cpp:35-82); ShapeError when incompatible."""
-    r = max(len(sa), len(sb))
+    r = _bi.max(len(sa), len(sb))
     pa = (1,) * (r - len(sa)) + tuple(sa)
     pb = (1,) * (r - len(sb)) + tuple(sb)
     out = []
@@ -120,7 +120,7 @@ def _byte_range(t: torch.Tensor):
     extent = 0
     for s, st in zip(t.shape, t.stride()):
         if s > 1 and st != 0:
-            extent += (s - 1) * abs(st) * es
+            extent += (s - 1) * _bi.abs(st) * es
     return base, base + extent + es
 
 

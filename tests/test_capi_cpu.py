@@ -98,10 +98,10 @@ def test_planner_hot_path_shapes():
     o4 = view(C, [64, 512, 1024])
     ft = view(C, [64, 512, 1024], [524288, 1, 512])
     assert plan_ew(C, o4, [view(C, [64, 512, 1024], dtype=2), ft])[0] == "tiled"
-    # config 4 div: P[64,512,1024] / D[1,512,1] -> rows with a per-row scalar
+    # config 4 div: P[64,512,1024] / D[1,512,1] -> rows of 256 packs with a per-row scalar
     o4d = view(C, [64, 512, 1024], dtype=1)
     assert plan_ew(C, o4d, [view(C, [64, 512, 1024]), view(C, [1, 512, 1], dtype=1)]) == \
-        ("rows_long", [64, 512, 1024])
+        ("rows_short", [64, 512, 1024])
     # config 5 fused chain: (X - r) * r with r [1, 8192]
     o5 = view(C, [32768, 8192])
     assert plan_ew(C, o5, [view(C, [32768, 8192]), view(C, [1, 8192]), view(C, [1, 8192])])[0] == "rows_long"
