@@ -4,10 +4,13 @@
 Workload (the multi-GPU configuration of the hot path): X float32 [262144, 8192] ~ N(0, 1)
 (seed 4), rows split into contiguous blocks across the ranks, and r float32 [1, 8192] ~ U(-1, 1)
 (seed 4, stream 1) on every rank. One step:
-    Y = (X - r) * r          fused into one pass, bit-identical to ctorch's sub then mul
+    Y = (X - r) * r          bit-identical to ctorch's sub then mul
     s = sum(Y)               float64 partial per rank, NCCL all-gather, rank-order combine
     k = argmin(Y, dim=1)     per row, first index on ties
-Total work is fixed as GPUs are added (strong scaling). `value` is elements of X processed per
+computed in one pass over each rank's rows (ctb_chain_rows: the chain with a row-argmin and
+float64-sum epilogue), then the 8-byte partials all-gathered. The same step as three kernels
+(chain, sum, argmin) and as ctorch's eager op sequence (sub, mul, sum, argmin) is timed too and
+reported beside it. Total work is fixed as GPUs are added (strong scaling). `value` is elements of X processed per
 second by the whole job, device-timed with CUDA events, max over ranks. Inputs (8 GiB in total)
 are larger than the 126 MB L2, so no flush is needed between steps.
 
@@ -178,13 +181,13 @@ def measured_peak():
 
 
 def ncu_traffic_per_row():
-    """DRAM bytes (read + write) per row of X for the fused elementwise kernel, from the committed
-    ncu summary (profiles/ncu_traffic.json), or None."""
+    """DRAM bytes (read + write) per row of X for the one-pass kernel, from the committed ncu
+    summary (profiles/ncu_traffic.json), or None."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(p) as f:
             d = json.load(f)
-        return float(d["chain_bytes"]) / float(d["chain_rows"])
+        return float(d["fused_rows_dram_bytes"]) / float(d["fused_rows_rows"])
     except (OSError, KeyError, ValueError, ZeroDivisionError):
         return None
 
@@ -198,7 +201,7 @@ def run_b200(args):
     import torch.distributed as dist
 
     import ctorch_b200 as cb
-    from ctorch_b200.sharded import ShardedSum, row_shard, sharded_step
+    from ctorch_b200.sharded import ShardedSum, row_shard, sharded_step_fused
     from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
 
     rank, world, local = env_rank()
@@ -236,7 +239,7 @@ def run_b200(args):
     torch.cuda.synchronize()
 
     def step():
-        return sharded_step(x, r, summer)
+        return sharded_step_fused(x, r, summer)
 
     for _ in range(args.warmup):
         step()
@@ -244,7 +247,7 @@ def run_b200(args):
     barrier()
 
     K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler()
     if rank == 0:
@@ -256,41 +259,45 @@ def run_b200(args):
     start.record()
     for i in range(K):
         ev[i][0].record()
-        y = cb.binary_chain("sub", "mul", x, r, r)
+        y, k, _ = cb.chain_rows("sub", "mul", x, r, r, row_op="min", out_sum=summer.partial)
         ev[i][1].record()
-        summer(y)
+        summer.combine()
         ev[i][2].record()
-        cb.argmin(y, 1)
-        ev[i][3].record()
-        del y
+        del y, k
     end.record()
     torch.cuda.synchronize()
     barrier()
     launches = cb.launch_count()
     clocks = sampler.stop() if rank == 0 else None
     elapsed = max_over_ranks(start.elapsed_time(end))
-    chain_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
-    sum_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
-    arg_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
-    chain_ms = max_over_ranks(chain_ms)
-    sum_ms = max_over_ranks(sum_ms)
-    arg_ms = max_over_ranks(arg_ms)
+    fused_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in ev))
+    comb_ms = max_over_ranks(statistics.mean(e[1].elapsed_time(e[2]) for e in ev))
     total_launches = int(sum_over_ranks(launches))
 
-    # eager drop-in sequence (sub then mul as two kernels) for comparison
-    eager_steps = min(K, 20)
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(eager_steps):
+    def time_steps(fn, n):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1)) / n
+
+    def three_kernels():
+        y = cb.binary_chain("sub", "mul", x, r, r)
+        summer(y)
+        cb.argmin(y, 1)
+
+    def eager_ops():
         y = cb.mul(cb.sub(x, r), r)
         summer(y)
         cb.argmin(y, 1)
-        del y
-    e1.record()
-    torch.cuda.synchronize()
-    eager_ms = max_over_ranks(e0.elapsed_time(e1)) / eager_steps
+
+    n_cmp = min(K, 20)
+    three_kernel_ms = time_steps(three_kernels, n_cmp)
+    eager_ms = time_steps(eager_ops, n_cmp)
 
     # end to end: pinned host input -> device, step, device -> pinned host results
     e2e = None
@@ -307,7 +314,7 @@ def run_b200(args):
         def e2e_step():
             xd.copy_(xh, non_blocking=True)
             rd.copy_(rh, non_blocking=True)
-            y, s, k = sharded_step(xd, rd, summer)
+            y, s, k = sharded_step_fused(xd, rd, summer)
             sh.copy_(s, non_blocking=True)
             kh.copy_(k, non_blocking=True)
 
@@ -326,8 +333,8 @@ def run_b200(args):
         e2e = {"value": ROWS * COLS / (e2e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": ROWS * COLS * 4 + world * COLS * 4,
                "d2h_bytes_per_step": ROWS * 8 + world * 4, "ms_per_step": e2e_ms,
-               "path": "pinned host X, r -> HBM; fused chain, sharded sum, argmin through the C ABI; "
-                       "s and k -> pinned host"}
+               "path": "pinned host X, r -> HBM; one-pass chain + row argmin + float64 partial "
+                       "(ctb_chain_rows), partials all-gathered and combined; s and k -> pinned host"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -340,8 +347,8 @@ def run_b200(args):
 
     if rank == 0:
         peak, peak_kind = measured_peak()
-        chain_bytes = shard.rows * COLS * 4 * 2 + COLS * 4
-        achieved = chain_bytes / (chain_ms / 1e3) / 1e9
+        fused_bytes = shard.rows * COLS * 4 * 2 + COLS * 4 + shard.rows * 8
+        achieved = fused_bytes / (fused_ms / 1e3) / 1e9
         tpr = ncu_traffic_per_row()
         ms_per_step = elapsed / K
         line = {
@@ -358,13 +365,14 @@ def run_b200(args):
             "dtype": "f32",
             "data": "synthetic",
             "config": base_config(world),
-            "gbs": ROWS * COLS * 4 * 4 / (ms_per_step / 1e3) / 1e9,
+            "gbs": (ROWS * COLS * 4 * 2 + ROWS * 8) / (ms_per_step / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "kernel": "fused (X - r) * r (ew_rows_long, FnChain)",
-                         "algorithmic_bytes": chain_bytes,
+                         "kernel": "fused_rows_kernel (ctb_chain_rows: (X - r) * r, row argmin, float64 sum)",
+                         "algorithmic_bytes": fused_bytes,
                          "traffic": tpr * shard.rows if tpr else None},
-            "kernels_ms": {"chain": chain_ms, "sum_allgather_combine": sum_ms, "argmin": arg_ms},
+            "kernels_ms": {"chain_rows": fused_ms, "allgather_combine": comb_ms},
+            "three_kernel_ms_per_step": three_kernel_ms,
             "eager_ms_per_step": eager_ms,
             "gpu_launches": total_launches,
             "clocks": clocks,
@@ -395,13 +403,14 @@ def run_case(args):
     rows = args.rows
     t = lambda shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
     case = args.case
-    if case in ("chain", "sum", "argmin", "sub"):
+    if case in ("chain", "sum", "argmin", "sub", "chain_rows"):
         x = device_fill(t((rows, COLS)), NORMAL, SEED, 0, 0.0, 1.0)
         r = device_fill(t((1, COLS)), UNIFORM, SEED, 1, -1.0, 1.0)
         y = cb.binary_chain("sub", "mul", x, r, r)
         summer = ShardedSum(dev, 1)
         fn = {"chain": lambda: cb.binary_chain("sub", "mul", x, r, r), "sub": lambda: cb.sub(x, r),
-              "sum": lambda: summer(y), "argmin": lambda: cb.argmin(y, 1)}[case]
+              "sum": lambda: summer(y), "argmin": lambda: cb.argmin(y, 1),
+              "chain_rows": lambda: cb.chain_rows("sub", "mul", x, r, r, out_sum=summer.partial)}[case]
     elif case in ("add", "relu"):
         a = device_fill(t((4096, 4096)), UNIFORM, 0, 0, -1.0, 1.0)
         b = device_fill(t((1, 4096)), UNIFORM, 0, 1, -1.0, 1.0)
@@ -438,7 +447,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--case", default=None,
-                    help="profiling mode: launch one kernel (chain, sub, sum, argmin, add, relu, sum_rows, "
+                    help="profiling mode: launch one kernel (chain_rows, chain, sub, sum, argmin, add, relu, sum_rows, "
                          "prod_rows, argmax_cols, max_cols, index_select, mul_t, div_b) --warmup + --steps times")
     ap.add_argument("--rows", type=int, default=16384, help="rows of X for --case (default 16384: 512 MiB)")
     args = ap.parse_args()

@@ -16,6 +16,7 @@ from .ops import (  # noqa: F401
     argmax,
     argmin,
     binary_chain,
+    chain_rows,
     broadcast_shape,
     div,
     div_,

@@ -69,6 +69,8 @@ def _load() -> ctypes.CDLL:
         "ctb_reduce_index_scratch_bytes": (sz, [P, i32]),
         "ctb_reduce_index": (i32, [i32, P, P, P, i32, vp, sz, vp]),
         "ctb_index_select": (i32, [P, i32, P, P, vp, vp]),
+        "ctb_chain_rows_scratch_bytes": (sz, [i32, i32, P, P, P, P, i32, P]),
+        "ctb_chain_rows": (i32, [i32, i32, P, P, P, P, i32, P, vp, vp, sz, vp]),
         "ctb_sum_partial_scratch_bytes": (sz, [P]),
         "ctb_sum_partial": (i32, [P, vp, vp, sz, vp]),
         "ctb_sum_combine": (i32, [vp, i32, P, vp]),

@@ -33,6 +33,11 @@ int index_select_dispatch(const ctb_view* src, int dim, const ctb_view* idx, con
                           int32_t* status, cudaStream_t st);
 int fill_random(const ctb_view* out, int dist, uint64_t seed, uint64_t stream_id, int64_t first,
                 double lo, double hi, cudaStream_t st);
+size_t fused_rows_scratch(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                          const ctb_view* y, int row_op, const ctb_view* idx);
+int fused_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+               const ctb_view* y, int row_op, const ctb_view* idx, double* d_sum, void* scratch,
+               size_t scratch_bytes, cudaStream_t st);
 
 namespace {
 thread_local std::string t_error;
@@ -337,6 +342,33 @@ int ctb_index_select(const ctb_view* src, int dim, const ctb_view* indices, cons
             if (out->shape[d] != want) return fail(CTB_ERR_SHAPE, "output shape mismatch");
         }
         return index_select_dispatch(src, dim, indices, out, d_status, static_cast<cudaStream_t>(stream));
+    });
+}
+
+size_t ctb_chain_rows_scratch_bytes(int op1, int op2, const ctb_view* a, const ctb_view* b,
+                                    const ctb_view* c, const ctb_view* y, int row_op,
+                                    const ctb_view* row_index) {
+    size_t need = 0;
+    guarded([&]() -> int {
+        if (check_views({a, b, c})) return CTB_ERR_ARGUMENT;
+        need = fused_rows_scratch(op1, op2, a, b, c, y, row_op, row_index);
+        return CTB_OK;
+    });
+    return need;
+}
+
+int ctb_chain_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                   const ctb_view* y, int row_op, const ctb_view* row_index, double* d_sum,
+                   void* scratch, size_t scratch_bytes, ctb_stream stream) {
+    return guarded([&]() -> int {
+        t_error.clear();
+        if (int rc = check_views({a, b, c})) return rc;
+        if (y)
+            if (int rc = check_views({y})) return rc;
+        if (row_index)
+            if (int rc = check_views({row_index})) return rc;
+        return fused_rows(op1, op2, a, b, c, y, row_op, row_index, d_sum, scratch, scratch_bytes,
+                          static_cast<cudaStream_t>(stream));
     });
 }
 

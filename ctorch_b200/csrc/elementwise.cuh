@@ -107,19 +107,34 @@ __global__ void __launch_bounds__(kEwBlock) ew_flat(EwArgs p, Fn fn) {
 }
 
 // ------------------------------------------------------------------------------------------------
-template <class Fn, class O, class I0, class I1, class I2, int NIN>
+// Which inputs are constant along the inner dim (stride 0): bit i for input i. BMASK >= 0 fixes it
+// at compile time, so a per-row scalar operand holds one register instead of a pack's worth;
+// BMASK < 0 reads it from the strides at run time.
+template <int BMASK, int NIN>
+__device__ __forceinline__ void inner_bcast(const EwArgs& p, bool& b0, bool& b1, bool& b2) {
+    const int r = p.rank - 1;
+    if constexpr (BMASK >= 0) {
+        b0 = BMASK & 1;
+        b1 = NIN > 1 && (BMASK & 2);
+        b2 = NIN > 2 && (BMASK & 4);
+    } else {
+        b0 = p.stride[1][r] == 0;
+        b1 = NIN > 1 && p.stride[2][r] == 0;
+        b2 = NIN > 2 && p.stride[3][r] == 0;
+    }
+}
+
+template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK>
 __device__ __forceinline__ void ew_row_segment(const EwArgs& p, const Fn& fn, const int64_t* off,
                                                int64_t c0, int64_t cstep, int count) {
     constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
     constexpr int U = kEwUnroll;
-    const int r = p.rank - 1;
     O* __restrict__ out = static_cast<O*>(p.out) + off[0];
     const I0* __restrict__ in0 = static_cast<const I0*>(p.in[0]) + off[1];
     const I1* __restrict__ in1 = static_cast<const I1*>(p.in[1]) + off[2];
     const I2* __restrict__ in2 = static_cast<const I2*>(p.in[2]) + off[3];
-    const bool b0 = p.stride[1][r] == 0;
-    const bool b1 = NIN > 1 && p.stride[2][r] == 0;
-    const bool b2 = NIN > 2 && p.stride[3][r] == 0;
+    bool b0, b1, b2;
+    inner_bcast<BMASK, NIN>(p, b0, b1, b2);
     const I0 s0 = b0 ? in0[0] : I0{};
     I1 s1{};
     I2 s2{};
@@ -152,8 +167,21 @@ __device__ __forceinline__ void ew_row_segment(const EwArgs& p, const Fn& fn, co
     }
 }
 
-template <class Fn, class O, class I0, class I1, class I2, int NIN>
-__global__ void __launch_bounds__(kEwBlock) ew_rows_long(EwArgs p, Fn fn) {
+// Min resident CTAs to ask of the register allocator: 4 when the packs live across the load
+// latency are small (<= 48 bytes per thread-pack), else 2.
+template <class O, class I0, class I1, class I2, int NIN, int BMASK> constexpr int rows_min_blocks() {
+    constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
+    if (BMASK < 0) return 2;
+    int bytes = V * static_cast<int>(sizeof(O));
+    if (!(BMASK & 1)) bytes += V * static_cast<int>(sizeof(I0));
+    if (NIN > 1 && !(BMASK & 2)) bytes += V * static_cast<int>(sizeof(I1));
+    if (NIN > 2 && !(BMASK & 4)) bytes += V * static_cast<int>(sizeof(I2));
+    return bytes <= 48 ? 4 : 2;
+}
+
+template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK>
+__global__ void __launch_bounds__(kEwBlock, (rows_min_blocks<O, I0, I1, I2, NIN, BMASK>()))
+    ew_rows_long(EwArgs p, Fn fn) {
     const int64_t seg = static_cast<int64_t>(kEwBlock) * kEwUnroll;
     const int64_t tiles = p.rows * static_cast<int64_t>(p.aux.d);
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -161,19 +189,18 @@ __global__ void __launch_bounds__(kEwBlock) ew_rows_long(EwArgs p, Fn fn) {
         p.aux.divmod(static_cast<uint64_t>(t), row, s);
         int64_t off[kMaxOps];
         ew_decode_row(p, row, NIN + 1, off);
-        ew_row_segment<Fn, O, I0, I1, I2, NIN>(p, fn, off, static_cast<int64_t>(s) * seg + threadIdx.x,
-                                               kEwBlock, kEwUnroll);
+        ew_row_segment<Fn, O, I0, I1, I2, NIN, BMASK>(p, fn, off, static_cast<int64_t>(s) * seg + threadIdx.x,
+                                                      kEwBlock, kEwUnroll);
     }
 }
 
-template <class Fn, class O, class I0, class I1, class I2, int NIN>
-__global__ void __launch_bounds__(kEwBlock) ew_rows_short(EwArgs p, Fn fn) {
+template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK>
+__global__ void __launch_bounds__(kEwBlock, (rows_min_blocks<O, I0, I1, I2, NIN, BMASK>()))
+    ew_rows_short(EwArgs p, Fn fn) {
     constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
     constexpr int U = kEwUnroll;
-    const int r = p.rank - 1;
-    const bool b0 = p.stride[1][r] == 0;
-    const bool b1 = NIN > 1 && p.stride[2][r] == 0;
-    const bool b2 = NIN > 2 && p.stride[3][r] == 0;
+    bool b0, b1, b2;
+    inner_bcast<BMASK, NIN>(p, b0, b1, b2);
     O* __restrict__ out = static_cast<O*>(p.out);
     const I0* __restrict__ in0 = static_cast<const I0*>(p.in[0]);
     const I1* __restrict__ in1 = static_cast<const I1*>(p.in[1]);
@@ -186,6 +213,9 @@ __global__ void __launch_bounds__(kEwBlock) ew_rows_short(EwArgs p, Fn fn) {
         Pack<I0, V> x0[U];
         Pack<I1, V> x1[U];
         Pack<I2, V> x2[U];
+        I0 s0[U];
+        I1 s1[U];
+        I2 s2[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int64_t v = base + u * nthr;
@@ -197,30 +227,15 @@ __global__ void __launch_bounds__(kEwBlock) ew_rows_short(EwArgs p, Fn fn) {
                 ew_decode_row(p, row, NIN + 1, off);
                 const int64_t cv = static_cast<int64_t>(c) * V;
                 oo[u] = off[0] + cv;
-                if (b0) {
-                    const I0 s = in0[off[1]];
-#pragma unroll
-                    for (int e = 0; e < V; ++e) x0[u].v[e] = s;
-                } else {
-                    x0[u] = load_pack<I0, V>(in0 + off[1] + cv);
-                }
+                if (b0) s0[u] = in0[off[1]];
+                else x0[u] = load_pack<I0, V>(in0 + off[1] + cv);
                 if constexpr (NIN > 1) {
-                    if (b1) {
-                        const I1 s = in1[off[2]];
-#pragma unroll
-                        for (int e = 0; e < V; ++e) x1[u].v[e] = s;
-                    } else {
-                        x1[u] = load_pack<I1, V>(in1 + off[2] + cv);
-                    }
+                    if (b1) s1[u] = in1[off[2]];
+                    else x1[u] = load_pack<I1, V>(in1 + off[2] + cv);
                 }
                 if constexpr (NIN > 2) {
-                    if (b2) {
-                        const I2 s = in2[off[3]];
-#pragma unroll
-                        for (int e = 0; e < V; ++e) x2[u].v[e] = s;
-                    } else {
-                        x2[u] = load_pack<I2, V>(in2 + off[3] + cv);
-                    }
+                    if (b2) s2[u] = in2[off[3]];
+                    else x2[u] = load_pack<I2, V>(in2 + off[3] + cv);
                 }
             }
         }
@@ -230,7 +245,9 @@ __global__ void __launch_bounds__(kEwBlock) ew_rows_short(EwArgs p, Fn fn) {
                 Pack<O, V> o;
 #pragma unroll
                 for (int e = 0; e < V; ++e)
-                    o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, x0[u].v[e], x1[u].v[e], x2[u].v[e]);
+                    o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, b0 ? s0[u] : x0[u].v[e],
+                                                              b1 ? s1[u] : x1[u].v[e],
+                                                              b2 ? s2[u] : x2[u].v[e]);
                 store_pack<O, V>(out + oo[u], o);
             }
         }
@@ -343,8 +360,132 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled(EwArgs p, Fn fn) {
     }
 }
 
+// Tiled with 4-element packs: the transposed input is read as packs of 4 along its unit-stride
+// dim p, the other input and the output as packs of 4 along the inner dim l, so a 64x64 tile costs
+// each thread 4 pack loads of each input and 4 pack stores. Edge tiles fall back to elements.
+// Requires (checked on the host, EwArgs::tiled_vec): pack-aligned bases and every stride other than
+// the unit ones a multiple of 4 elements; the row-major input has unit inner stride.
+template <class Fn, class O, class I0, class I1, int XOP>
+__global__ void __launch_bounds__(kEwBlock) ew_tiled4(EwArgs p, Fn fn) {
+    using X = std::conditional_t<XOP == 1, I0, I1>;
+    using Y = std::conditional_t<XOP == 1, I1, I0>;
+    constexpr int YOP = XOP == 1 ? 2 : 1;
+    constexpr int kPer = kTile * kTile / 4 / kEwBlock;  // packs per thread (4)
+    __shared__ X tile[kTile][kTile + 1];
+    const int r = p.rank - 1;
+    const int pd = p.pdim;
+    const int64_t L = p.shape[r];
+    const int64_t P = p.shape[pd];
+    const int64_t sXl = p.stride[XOP][r];
+    const int64_t sYp = p.stride[YOP][pd];
+    const int64_t sOp = p.stride[0][pd];
+    const X* __restrict__ xin = static_cast<const X*>(p.in[XOP - 1]);
+    const Y* __restrict__ yin = static_cast<const Y*>(p.in[YOP - 1]);
+    O* __restrict__ out = static_cast<O*>(p.out);
+    const int64_t tiles_l = static_cast<int64_t>(p.aux.d);
+    const int64_t tiles_p = static_cast<int64_t>(p.aux2.d);
+    const int64_t total = (p.n / (L * P)) * tiles_l * tiles_p;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        uint64_t rest, tl, batch, tp;
+        p.aux.divmod(static_cast<uint64_t>(t), rest, tl);
+        p.aux2.divmod(rest, batch, tp);
+        int64_t offO = 0, offX = 0, offY = 0;
+        for (int d = r - 1; d >= 0; --d) {
+            if (d == pd) continue;
+            uint64_t q, c;
+            p.div[d].divmod(batch, q, c);
+            offO += static_cast<int64_t>(c) * p.stride[0][d];
+            offX += static_cast<int64_t>(c) * p.stride[XOP][d];
+            offY += static_cast<int64_t>(c) * p.stride[YOP][d];
+            batch = q;
+        }
+        const int64_t l0 = static_cast<int64_t>(tl) * kTile;
+        const int64_t p0 = static_cast<int64_t>(tp) * kTile;
+        const bool full = p0 + kTile <= P && l0 + kTile <= L;
+        if (full) {
+            const X* xt = xin + offX + p0 + l0 * sXl;
+            const Y* yt = yin + offY + p0 * sYp + l0;
+            O* ot = out + offO + p0 * sOp + l0;
+            Pack<X, 4> xr[kPer];
+            Pack<Y, 4> yr[kPer];
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int k = threadIdx.x + j * kEwBlock;
+                const int li = k >> 4, pg = k & 15;  // X: pack pg of row li (along p)
+                xr[j] = load_pack<X, 4>(xt + 4 * pg + li * sXl);
+            }
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int k = threadIdx.x + j * kEwBlock;
+                const int pi = k >> 4, lg = k & 15;  // Y: pack lg of row pi (along l)
+                yr[j] = load_pack<Y, 4>(yt + pi * sYp + 4 * lg);
+            }
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int k = threadIdx.x + j * kEwBlock;
+                const int li = k >> 4, pg = k & 15;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) tile[li][4 * pg + e] = xr[j].v[e];
+            }
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int k = threadIdx.x + j * kEwBlock;
+                const int pi = k >> 4, lg = k & 15;
+                Pack<O, 4> o;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const X x = tile[4 * lg + e][pi];
+                    if constexpr (XOP == 1) o.v[e] = fn(x, yr[j].v[e]);
+                    else o.v[e] = fn(yr[j].v[e], x);
+                }
+                store_pack<O, 4>(ot + pi * sOp + 4 * lg, o);
+            }
+            __syncthreads();
+        } else {
+            for (int k = threadIdx.x; k < kTile * kTile; k += kEwBlock) {
+                const int li = k >> 6, pi = k & 63;
+                const int64_t pp = p0 + pi, ll = l0 + li;
+                if (pp < P && ll < L) tile[li][pi] = xin[offX + pp + ll * sXl];
+            }
+            __syncthreads();
+            for (int k = threadIdx.x; k < kTile * kTile; k += kEwBlock) {
+                const int pi = k >> 6, li = k & 63;
+                const int64_t pp = p0 + pi, ll = l0 + li;
+                if (pp < P && ll < L) {
+                    const X x = tile[li][pi];
+                    const Y y = yin[offY + pp * sYp + ll];
+                    O o;
+                    if constexpr (XOP == 1) o = fn(x, y);
+                    else o = fn(y, x);
+                    out[offO + pp * sOp + ll] = o;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
 // ------------------------------------------------------------------------------------------------
 // Launcher. Returns a ctb_status.
+
+// One wave of resident CTAs of `kernel` (grid-stride loops cover the rest): no tail of a partly
+// filled second wave.
+template <class K> inline unsigned wave_grid(K kernel, int64_t work) {
+    const int64_t slots = static_cast<int64_t>(sm_count()) *
+                          resident_ctas(reinterpret_cast<const void*>(kernel), kEwBlock);
+    const int64_t g = work < slots ? work : slots;
+    return static_cast<unsigned>(g < 1 ? 1 : g);
+}
+
+// Bit i set when input i has stride 0 along the inner dim.
+inline int inner_mask(const EwArgs& a, int nin) {
+    int m = 0;
+    for (int i = 0; i < nin; ++i)
+        if (a.stride[1 + i][a.rank - 1] == 0) m |= 1 << i;
+    return m;
+}
+
 template <class Fn, class O, class I0, class I1 = I0, class I2 = I0, int NIN = 1>
 int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
     constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
@@ -355,17 +496,45 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
     case EwPath::Flat: {
         const int64_t nvec = a.n / V;
         const int64_t work = (nvec + kEwBlock * kEwUnroll - 1) / (kEwBlock * kEwUnroll);
-        ew_flat<Fn, O, I0, I1, I2, NIN><<<grid_for(work < 1 ? 1 : work, 16), kEwBlock, 0, st>>>(a, fn);
+        auto k = &ew_flat<Fn, O, I0, I1, I2, NIN>;
+        k<<<wave_grid(k, work), kEwBlock, 0, st>>>(a, fn);
         break;
     }
     case EwPath::RowsLong: {
         const int64_t tiles = a.rows * static_cast<int64_t>(a.aux.d);
-        ew_rows_long<Fn, O, I0, I1, I2, NIN><<<grid_for(tiles, 16), kEwBlock, 0, st>>>(a, fn);
+#define CTB_RL(M)                                                        \
+    {                                                                    \
+        auto k = &ew_rows_long<Fn, O, I0, I1, I2, NIN, M>;               \
+        k<<<wave_grid(k, tiles), kEwBlock, 0, st>>>(a, fn);              \
+    }
+        switch (inner_mask(a, NIN)) {
+        case 0: CTB_RL(0) break;
+        case 1: CTB_RL(1) break;
+        case 2:
+            if constexpr (NIN > 1) { CTB_RL(2) break; }
+            [[fallthrough]];
+        default: CTB_RL(-1) break;
+        }
+#undef CTB_RL
         break;
     }
     case EwPath::RowsShort: {
         const int64_t nvec = a.rows * a.vpr;
-        ew_rows_short<Fn, O, I0, I1, I2, NIN><<<grid_for((nvec + kEwBlock * kEwUnroll - 1) / (kEwBlock * kEwUnroll), 16), kEwBlock, 0, st>>>(a, fn);
+        const int64_t work = (nvec + kEwBlock * kEwUnroll - 1) / (kEwBlock * kEwUnroll);
+#define CTB_RS(M)                                                        \
+    {                                                                    \
+        auto k = &ew_rows_short<Fn, O, I0, I1, I2, NIN, M>;              \
+        k<<<wave_grid(k, work), kEwBlock, 0, st>>>(a, fn);               \
+    }
+        switch (inner_mask(a, NIN)) {
+        case 0: CTB_RS(0) break;
+        case 1: CTB_RS(1) break;
+        case 2:
+            if constexpr (NIN > 1) { CTB_RS(2) break; }
+            [[fallthrough]];
+        default: CTB_RS(-1) break;
+        }
+#undef CTB_RS
         break;
     }
     case EwPath::Tiled: {
@@ -373,10 +542,19 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
             const int64_t L = a.shape[a.rank - 1];
             const int64_t P = a.shape[a.pdim];
             const int64_t total = (a.n / (L * P)) * static_cast<int64_t>(a.aux.d) * static_cast<int64_t>(a.aux2.d);
-            if (a.xop == 1)
+            if (a.tiled_vec) {
+                if (a.xop == 1) {
+                    auto k = &ew_tiled4<Fn, O, I0, I1, 1>;
+                    k<<<wave_grid(k, total), kEwBlock, 0, st>>>(a, fn);
+                } else {
+                    auto k = &ew_tiled4<Fn, O, I0, I1, 2>;
+                    k<<<wave_grid(k, total), kEwBlock, 0, st>>>(a, fn);
+                }
+            } else if (a.xop == 1) {
                 ew_tiled<Fn, O, I0, I1, 1><<<grid_for(total, 16), kEwBlock, 0, st>>>(a, fn);
-            else
+            } else {
                 ew_tiled<Fn, O, I0, I1, 2><<<grid_for(total, 16), kEwBlock, 0, st>>>(a, fn);
+            }
             break;
         }
         [[fallthrough]];

@@ -1,0 +1,318 @@
+// fused_rows.cu — one pass over a row-major matrix that computes an elementwise chain and reduces
+// its result two ways in the epilogue:
+//     y = op2(op1(a, b), c)              (written, bit-identical to the two eager ops)
+//     idx[row] = arg{min,max}(y[row, :]) (first index on ties, first NaN wins)
+//     partial  = sum(y) in float64       (deterministic: fixed per-CTA order, then CTA order)
+// a is [R, C] with unit inner stride; b and c are [C] rows broadcast over R (or 0-d scalars).
+// One warp per row, persistent grid of one wave; each lane keeps its running extreme with a strict
+// compare (so its first occurrence wins without carrying the index through every compare), and the
+// lanes' (value, index) states are combined by warp shuffles with the full tie/NaN rule of
+// src/ops/reduction_functors.h:55-110. Reads a once and writes y once: the eager sequence
+// (chain, then sum, then argmin) reads y twice more.
+#include <limits>
+
+#include "common.cuh"
+#include "plan.cuh"
+
+namespace ctb {
+
+struct FusedRowsArgs {
+    const void* a;
+    const void* b;
+    const void* c;
+    void* y;          // may be null
+    int64_t* idx;     // may be null
+    double* partials; // per-CTA sums (scratch), may be null
+    int64_t rows, cols;
+    int64_t a_row_stride, y_row_stride, idx_stride;
+    int b_bcast, c_bcast;  // 1: b/c is a 0-d scalar (stride 0 along the row)
+    int c_is_b;
+    int is_max;
+};
+
+template <class T> __device__ __forceinline__ T extreme_ident(bool is_max) {
+    return is_max ? -std::numeric_limits<T>::infinity() : std::numeric_limits<T>::infinity();
+}
+
+// STAGE: b and c are copied once per CTA into shared memory (a 0-d scalar is expanded to a row),
+// so the per-element reads of the broadcast row never hold registers across the latency of the
+// loads of a; without STAGE (rows too long for shared memory) they are read through L1.
+template <int OP1, int OP2, class T, int V, bool STAGE>
+__global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
+    constexpr int U = 4;
+    extern __shared__ __align__(16) unsigned char fr_smem[];
+    const int lane = threadIdx.x & 31;
+    const int C = static_cast<int>(p.cols);
+    const T* __restrict__ B = static_cast<const T*>(p.b);
+    const T* __restrict__ Cc = static_cast<const T*>(p.c);
+    if constexpr (STAGE) {
+        T* sb = reinterpret_cast<T*>(fr_smem);
+        constexpr int kPad = 16 / sizeof(T);  // keep the second row 16-byte aligned
+        T* sc = sb + (p.c_is_b ? 0 : (C + kPad - 1) / kPad * kPad);
+        const T b0 = p.b_bcast ? B[0] : T(0);
+        const T c0 = p.c_bcast ? Cc[0] : T(0);
+        for (int j = threadIdx.x; j < C; j += blockDim.x) {
+            sb[j] = p.b_bcast ? b0 : B[j];
+            if (!p.c_is_b) sc[j] = p.c_bcast ? c0 : Cc[j];
+        }
+        __syncthreads();
+        B = sb;
+        Cc = sc;
+    }
+    const bool b_row = STAGE || !p.b_bcast;
+    const bool c_row = STAGE || !p.c_bcast;
+    const T* __restrict__ A = static_cast<const T*>(p.a);
+    T* __restrict__ Y = static_cast<T*>(p.y);
+    const bool is_max = p.is_max != 0;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int nv = C / V;  // whole packs per row (V == 1 when rows are not pack-aligned)
+    double sum = 0.0;
+
+    for (int64_t row = warp; row < p.rows; row += nwarps) {
+        const T* ar = A + row * p.a_row_stride;
+        T* yr = Y ? Y + row * p.y_row_stride : nullptr;
+        T best = extreme_ident<T>(is_max);
+        int bidx = -1;
+        for (int v0 = lane; v0 < nv; v0 += 32 * U) {
+            Pack<T, V> xa[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int v = v0 + u * 32;
+                if (v < nv) xa[u] = load_pack<T, V>(ar + static_cast<int64_t>(v) * V);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int v = v0 + u * 32;
+                if (v < nv) {
+                    Pack<T, V> xb, xc, o;
+                    if (b_row) xb = *reinterpret_cast<const Pack<T, V>*>(B + v * V);
+                    if (!p.c_is_b && c_row) xc = *reinterpret_cast<const Pack<T, V>*>(Cc + v * V);
+#pragma unroll
+                    for (int e = 0; e < V; ++e) {
+                        const T bb = b_row ? xb.v[e] : B[0];
+                        const T cc = p.c_is_b ? bb : (c_row ? xc.v[e] : Cc[0]);
+                        const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(xa[u].v[e], bb), cc);
+                        o.v[e] = yv;
+                        sum = __dadd_rn(sum, static_cast<double>(yv));
+                        const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
+                        if (repl) {
+                            best = yv;
+                            bidx = v * V + e;
+                        }
+                    }
+                    if (yr) store_pack<T, V>(yr + static_cast<int64_t>(v) * V, o);
+                }
+            }
+        }
+        // scalar tail (columns past the last whole pack)
+        for (int j = nv * V + lane; j < C; j += 32) {
+            const T bb = b_row ? B[j] : B[0];
+            const T cc = p.c_is_b ? bb : (c_row ? Cc[j] : Cc[0]);
+            const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(ar[j], bb), cc);
+            if (yr) yr[j] = yv;
+            sum = __dadd_rn(sum, static_cast<double>(yv));
+            const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
+            if (repl) {
+                best = yv;
+                bidx = j;
+            }
+        }
+        if (p.idx) {
+            // Combine lanes: NaN first (lowest index), then the extreme value, then the lower
+            // index. A lane that saw only +-inf (the min/max identity) keeps index -1 = "empty".
+#pragma unroll
+            for (int m = 16; m >= 1; m >>= 1) {
+                const T ov = __shfl_xor_sync(0xffffffffu, best, m);
+                const int oi = __shfl_xor_sync(0xffffffffu, bidx, m);
+                bool take;
+                if (oi < 0) take = false;
+                else if (bidx < 0) take = true;
+                else {
+                    const bool an = best != best, bn = ov != ov;
+                    if (an || bn) take = an ? (bn && oi < bidx) : true;
+                    else if (is_max ? ov > best : ov < best) take = true;
+                    else take = (ov == best) && oi < bidx;
+                }
+                if (take) {
+                    best = ov;
+                    bidx = oi;
+                }
+            }
+            // every element equal to the identity (+inf for min, -inf for max): the first one wins
+            if (lane == 0) p.idx[row * p.idx_stride] = bidx < 0 ? 0 : bidx;
+        }
+    }
+    if (p.partials) {
+        __shared__ double sm[8];
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, m));
+        if (lane == 0) sm[threadIdx.x >> 5] = sum;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double s = 0.0;
+            for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s = __dadd_rn(s, sm[w]);
+            p.partials[blockIdx.x] = s;
+        }
+    }
+}
+
+__global__ void fused_rows_combine(const double* partials, int n, double* out) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    double s = 0.0;
+    for (int i = 0; i < n; ++i) s = __dadd_rn(s, partials[i]);
+    *out = s;
+}
+
+template <int OP1, int OP2, class T>
+static const void* pick_kernel(bool vec, bool stage) {
+    constexpr int V = 16 / sizeof(T);
+    if (stage)
+        return vec ? reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, true>)
+                   : reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, 1, true>);
+    return vec ? reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, false>)
+               : reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, 1, false>);
+}
+
+template <int OP1, int OP2, class T>
+static void launch_typed(bool vec, bool stage, unsigned grid, size_t smem, const FusedRowsArgs& p,
+                         cudaStream_t st) {
+    constexpr int V = 16 / sizeof(T);
+    if (stage) {
+        if (vec) fused_rows_kernel<OP1, OP2, T, V, true><<<grid, 256, smem, st>>>(p);
+        else fused_rows_kernel<OP1, OP2, T, 1, true><<<grid, 256, smem, st>>>(p);
+    } else {
+        if (vec) fused_rows_kernel<OP1, OP2, T, V, false><<<grid, 256, 0, st>>>(p);
+        else fused_rows_kernel<OP1, OP2, T, 1, false><<<grid, 256, 0, st>>>(p);
+    }
+}
+
+template <class T>
+static void launch_ops(int op1, int op2, bool vec, bool stage, unsigned grid, size_t smem,
+                       const FusedRowsArgs& p, cudaStream_t st, const void** fn_out) {
+#define CTB_FR(O1, O2)                                                            \
+    if (op1 == O1 && op2 == O2) {                                                 \
+        if (fn_out) *fn_out = pick_kernel<O1, O2, T>(vec, stage);                 \
+        else launch_typed<O1, O2, T>(vec, stage, grid, smem, p, st);              \
+        return;                                                                   \
+    }
+    CTB_FR(CTB_SUB, CTB_MUL) CTB_FR(CTB_ADD, CTB_MUL) CTB_FR(CTB_MUL, CTB_ADD) CTB_FR(CTB_SUB, CTB_DIV)
+    CTB_FR(CTB_ADD, CTB_ADD) CTB_FR(CTB_SUB, CTB_SUB) CTB_FR(CTB_MUL, CTB_MUL) CTB_FR(CTB_DIV, CTB_DIV)
+    CTB_FR(CTB_ADD, CTB_SUB) CTB_FR(CTB_ADD, CTB_DIV) CTB_FR(CTB_SUB, CTB_ADD) CTB_FR(CTB_MUL, CTB_SUB)
+    CTB_FR(CTB_MUL, CTB_DIV) CTB_FR(CTB_DIV, CTB_ADD) CTB_FR(CTB_DIV, CTB_SUB) CTB_FR(CTB_DIV, CTB_MUL)
+#undef CTB_FR
+}
+
+// Largest staged footprint (b and c rows) that still leaves room for two CTAs per SM.
+constexpr size_t kMaxStageBytes = 96 * 1024;
+
+// Validation + planning shared by the scratch query and the launch. Returns the grid.
+static int plan_fused(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                      const ctb_view* y, int row_op, const ctb_view* idx, FusedRowsArgs& p,
+                      bool& vec, bool& stage, size_t& smem, unsigned& grid) {
+    if (op1 < CTB_ADD || op1 > CTB_DIV || op2 < CTB_ADD || op2 > CTB_DIV)
+        return fail(CTB_ERR_ARGUMENT, "unknown binary op");
+    if (row_op != CTB_MIN && row_op != CTB_MAX) return fail(CTB_ERR_ARGUMENT, "row_op must be CTB_MIN or CTB_MAX");
+    const int dt = a->dtype;
+    if (dt != CTB_FLOAT32 && dt != CTB_FLOAT64) return fail(CTB_ERR_DTYPE, "fused rows take float32/float64");
+    if (b->dtype != dt || c->dtype != dt || (y && y->dtype != dt))
+        return fail(CTB_ERR_DTYPE, "fused rows take operands of one dtype");
+    if (idx && idx->dtype != CTB_INT64) return fail(CTB_ERR_DTYPE, "row indices must be int64");
+    if (a->ndim != 2 || a->strides[1] != 1 || a->shape[0] < 0 || a->shape[1] < 1)
+        return fail(CTB_ERR_SHAPE, "a must be a 2-D [rows, cols] view with unit inner stride and cols >= 1");
+    const int64_t R = a->shape[0], C = a->shape[1];
+    if (C >= (int64_t(1) << 31)) return fail(CTB_ERR_SHAPE, "rows of 2^31 or more columns are not supported");
+    auto row_operand = [&](const ctb_view* v, int& bcast) -> bool {
+        int64_t n = 1;
+        for (int d = 0; d < v->ndim; ++d) n *= v->shape[d];
+        if (n == 1) {
+            bcast = 1;
+            return true;
+        }
+        bcast = 0;
+        if (n != C) return false;
+        // [C] or [1, C] with unit stride on the C dim
+        for (int d = 0; d < v->ndim; ++d)
+            if (v->shape[d] == C && v->strides[d] != 1) return false;
+        return true;
+    };
+    if (!row_operand(b, p.b_bcast) || !row_operand(c, p.c_bcast))
+        return fail(CTB_ERR_SHAPE, "b and c must be one contiguous row of `cols` elements, or scalars");
+    if (y && (y->ndim != 2 || y->shape[0] != R || y->shape[1] != C || y->strides[1] != 1))
+        return fail(CTB_ERR_SHAPE, "y must be a [rows, cols] view with unit inner stride");
+    if (idx && !((idx->ndim == 1 && idx->shape[0] == R) || (idx->ndim == 2 && idx->shape[0] == R && idx->shape[1] == 1)))
+        return fail(CTB_ERR_SHAPE, "row indices must be [rows] or [rows, 1]");
+    p.a = a->data;
+    p.b = b->data;
+    p.c = c->data;
+    p.y = y ? y->data : nullptr;
+    p.idx = idx ? static_cast<int64_t*>(idx->data) : nullptr;
+    p.rows = R;
+    p.cols = C;
+    p.a_row_stride = a->strides[0];
+    p.y_row_stride = y ? y->strides[0] : 0;
+    p.idx_stride = idx ? idx->strides[0] : 0;
+    p.c_is_b = (c->data == b->data && p.c_bcast == p.b_bcast) ? 1 : 0;
+    p.is_max = row_op == CTB_MAX;
+    const int es = static_cast<int>(dtype_size(dt));
+    vec = aligned16(a->data) && (!y || aligned16(y->data)) && (p.b_bcast || aligned16(b->data)) &&
+          (p.c_bcast || aligned16(c->data)) && (p.a_row_stride * es) % 16 == 0 &&
+          (!y || (p.y_row_stride * es) % 16 == 0);
+    const size_t row_bytes = static_cast<size_t>((C * es + 15) / 16 * 16);
+    smem = (p.c_is_b ? 1 : 2) * row_bytes;
+    stage = smem <= kMaxStageBytes;
+    if (!stage) smem = 0;
+    const void* fn = nullptr;
+    if (dt == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, 0, smem, p, nullptr, &fn);
+    else launch_ops<double>(op1, op2, vec, stage, 0, smem, p, nullptr, &fn);
+    if (smem > 48 * 1024) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+            return check_launch("fused rows smem attribute");
+    }
+    const int64_t slots = static_cast<int64_t>(sm_count()) * resident_ctas(fn, 256, smem);
+    const int64_t ctas = (R + 7) / 8;
+    grid = static_cast<unsigned>(ctas < 1 ? 1 : (ctas < slots ? ctas : slots));
+    return CTB_OK;
+}
+
+size_t fused_rows_scratch(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                          const ctb_view* y, int row_op, const ctb_view* idx) {
+    FusedRowsArgs p{};
+    bool vec, stage;
+    size_t smem;
+    unsigned grid;
+    if (plan_fused(op1, op2, a, b, c, y, row_op, idx, p, vec, stage, smem, grid)) return 0;
+    return static_cast<size_t>(grid) * sizeof(double);
+}
+
+int fused_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+               const ctb_view* y, int row_op, const ctb_view* idx, double* d_sum, void* scratch,
+               size_t scratch_bytes, cudaStream_t st) {
+    FusedRowsArgs p{};
+    bool vec, stage;
+    size_t smem;
+    unsigned grid;
+    if (int rc = plan_fused(op1, op2, a, b, c, y, row_op, idx, p, vec, stage, smem, grid)) return rc;
+    if (d_sum) {
+        const size_t need = static_cast<size_t>(grid) * sizeof(double);
+        if (!scratch || scratch_bytes < need)
+            return fail(CTB_ERR_SCRATCH, "scratch buffer too small: need " + std::to_string(need) + " bytes");
+        p.partials = static_cast<double*>(scratch);
+    }
+    if (p.rows == 0) {
+        if (d_sum && cudaMemsetAsync(d_sum, 0, sizeof(double), st) != cudaSuccess)
+            return check_launch("fused rows");
+        return CTB_OK;
+    }
+    if (a->dtype == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
+    else launch_ops<double>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
+    int launches = 1;
+    if (d_sum) {
+        fused_rows_combine<<<1, 32, 0, st>>>(p.partials, static_cast<int>(grid), d_sum);
+        ++launches;
+    }
+    count_launch(launches);
+    return check_launch("fused rows");
+}
+
+}  // namespace ctb

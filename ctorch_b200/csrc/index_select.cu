@@ -60,7 +60,7 @@ __device__ __forceinline__ int64_t resolve(const GatherArgs& p, int64_t j) {
 
 // Warp per output row; U rows in flight per warp; unit VB bytes.
 template <class I, class VT>
-__global__ void __launch_bounds__(256) gather_rows(GatherArgs p) {
+__global__ void __launch_bounds__(256, 4) gather_rows(GatherArgs p) {
     constexpr int U = 4;
     constexpr int VB = sizeof(VT);
     if (*reinterpret_cast<volatile int32_t*>(p.status) != 0) return;

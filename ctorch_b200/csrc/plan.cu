@@ -202,6 +202,20 @@ int plan_elementwise(const ctb_view* out, const ctb_view* const* ins, int nin, c
         if (others_ok && xop != -1 && pdim != -1) {
             a.xop = xop;
             a.pdim = pdim;
+            // 4-element packs: every operand's base aligned to its pack (16 B for 4-byte types,
+            // 32 B for 8-byte types -> 16 B suffices for whole-chunk access), the row-major input
+            // unit-stride on the inner dim, and every other stride a multiple of 4 elements.
+            const int yop = xop == 1 ? (s.nops > 2 ? 2 : -1) : 1;
+            bool v4 = yop > 0 && s.stride[yop][r - 1] == 1;
+            for (int o = 0; o < s.nops && v4; ++o) {
+                if (!aligned16(base[o])) v4 = false;
+                for (int d = 0; d < r; ++d) {
+                    const int64_t st = s.stride[o][d];
+                    const bool unit = (o == xop && d == pdim) || (o != xop && d == r - 1);
+                    if (!unit && st % 4 != 0) v4 = false;
+                }
+            }
+            a.tiled_vec = v4 ? 1 : 0;
             constexpr int kTile = 64;
             a.aux = FastDiv(static_cast<uint64_t>((a.L + kTile - 1) / kTile));
             a.aux2 = FastDiv(static_cast<uint64_t>((s.shape[pdim] + kTile - 1) / kTile));

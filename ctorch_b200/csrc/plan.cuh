@@ -43,6 +43,7 @@ struct EwArgs {
     int rank;
     int xop;                       // Tiled: which input (1..3) is read transposed
     int pdim;                      // Tiled: the dim on which that input has stride 1
+    int tiled_vec;                 // Tiled: 4-element packs are aligned (ew_tiled4)
     int64_t n;                     // total elements
     int64_t L;                     // innermost extent
     int64_t rows;                  // n / L

@@ -129,19 +129,30 @@ template <class T, bool IsMax, bool Indexed> struct RMinMax {
         if (IsMax ? (bv > a.v) : (bv < a.v)) return true;
         return bv == a.v && bi < a.i;
     }
+    // Every kernel folds a thread's elements in increasing position order, so a strict compare
+    // keeps the first occurrence and a NaN, once adopted, is kept (the sequential CPU rule). A
+    // state that has only met the identity value (+-inf, or the integer limit) keeps the "empty"
+    // position INT64_MAX; `combine` applies the full rule, and `write` maps an all-identity
+    // slice to position 0, its first element.
     __device__ __forceinline__ static void fold(State& s, T v, int64_t j) {
-        if (better(s, v, j)) {
+        bool take;
+        if constexpr (is_float_v<T>) take = (s.v == s.v) && ((v != v) || (IsMax ? v > s.v : v < s.v));
+        else take = IsMax ? v > s.v : v < s.v;
+        if (take) {
             s.v = v;
             s.i = j;
         }
     }
-    __device__ __forceinline__ static void combine(State& a, const State& b) { fold(a, b.v, b.i); }
+    __device__ __forceinline__ static void combine(State& a, const State& b) {
+        if (better(a, b.v, b.i)) a = b;
+    }
     __device__ __forceinline__ static State shfl(const State& s, int m) {
         return State{shfl_xor(s.v, m), shfl_xor(s.i, m)};
     }
     __device__ __forceinline__ static void write(const RedArgs& p, const State& s, int64_t o1, int64_t o2) {
         if (p.out) static_cast<T*>(p.out)[o1] = s.v;
-        if constexpr (Indexed) static_cast<int64_t*>(p.out2)[o2] = s.i;
+        if constexpr (Indexed)
+            static_cast<int64_t*>(p.out2)[o2] = s.i == std::numeric_limits<int64_t>::max() ? 0 : s.i;
     }
 };
 

@@ -186,6 +186,31 @@ def binary_chain(op1: str, op2: str, a, b, c) -> torch.Tensor:
     return out
 
 
+def chain_rows(op1: str, op2: str, a, b, c, row_op: str = "min", write_y: bool = True,
+               want_sum: bool = True, out_sum: torch.Tensor | None = None):
+    """One pass over a [rows, cols] matrix: y = op2(op1(a, b), c) with b, c one broadcast row,
+    plus the per-row argmin/argmax of y and the float64 sum of y (ctb_chain_rows). Returns
+    (y or None, row indices int64 [rows], float64 sum tensor [1] or None). y and the indices are
+    bit-identical to the eager ops; the sum matches to float64 rounding."""
+    codes = {"add": C.ADD, "sub": C.SUB, "mul": C.MUL, "div": C.DIV}
+    dev = _cuda("chain_rows", a, b, c)
+    y = torch.empty(a.shape, dtype=a.dtype, device=dev) if write_y else None
+    idx = torch.empty(a.shape[0], dtype=torch.int64, device=dev)
+    s = None
+    if want_sum:
+        s = out_sum if out_sum is not None else torch.empty(1, dtype=torch.float64, device=dev)
+    rop = C.MIN if row_op == "min" else C.MAX
+    with torch.cuda.device(dev):
+        va, vb, vc, vy, vi = C.view(a), C.view(b), C.view(c), C.view(y), C.view(idx)
+        need = C.lib.ctb_chain_rows_scratch_bytes(codes[op1], codes[op2], va, vb, vc, vy, rop, vi) if want_sum else 0
+        scratch = _scratch(need, dev)
+        _call(C.lib.ctb_chain_rows(codes[op1], codes[op2], va, vb, vc, vy, rop, vi,
+                                   s.data_ptr() if s is not None else None,
+                                   scratch.data_ptr() if scratch is not None else None, need,
+                                   C.stream_handle(dev)), "chain_rows")
+    return y, idx, s
+
+
 def _unary(op: int, x: torch.Tensor, name: str) -> torch.Tensor:
     dev = _cuda(name, x)
     out = torch.empty(x.shape, dtype=x.dtype, device=dev)

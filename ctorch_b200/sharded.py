@@ -77,6 +77,10 @@ class ShardedSum:
 
     def __call__(self, local: torch.Tensor) -> torch.Tensor:
         self.partial_fn(local, self.partial)
+        return self.combine()
+
+    def combine(self) -> torch.Tensor:
+        """All-gathers self.partial (already written by this rank) and combines in rank order."""
         if self.world > 1:
             import torch.distributed as dist
 
@@ -96,4 +100,16 @@ def sharded_step(x_local: torch.Tensor, r: torch.Tensor, summer: ShardedSum):
     y = binary_chain("sub", "mul", x_local, r, r)
     s = summer(y)
     k = argmin(y, 1)
+    return y, s, k
+
+
+def sharded_step_fused(x_local: torch.Tensor, r: torch.Tensor, summer: ShardedSum):
+    """The same step in one pass over this rank's rows (ctb_chain_rows): Y written, the per-row
+    argmin and this rank's float64 partial produced in the epilogue, then the 8-byte partials
+    all-gathered and combined in rank order. Y and k are bit-identical to sharded_step; s matches
+    it to float64 rounding of the partials."""
+    from .ops import chain_rows
+
+    y, k, _ = chain_rows("sub", "mul", x_local, r, r, row_op="min", out_sum=summer.partial)
+    s = summer.combine()
     return y, s, k

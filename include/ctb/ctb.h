@@ -151,6 +151,28 @@ CTB_API int ctb_reduce_index(int op, const ctb_view* in, const ctb_view* values,
 CTB_API int ctb_index_select(const ctb_view* src, int dim, const ctb_view* indices, const ctb_view* out,
                      int32_t* d_status, ctb_stream stream);
 
+/* ---- single-pass chain + row reductions ---- */
+
+/* Scratch bytes for ctb_chain_rows (0 when d_sum is not wanted). */
+CTB_API size_t ctb_chain_rows_scratch_bytes(int op1, int op2, const ctb_view* a, const ctb_view* b,
+                                            const ctb_view* c, const ctb_view* y, int row_op,
+                                            const ctb_view* row_index);
+
+/* One pass over a [rows, cols] matrix a (unit inner stride) with b and c one broadcast row of
+ * cols elements (or 0-d scalars), all float32 or all float64:
+ *     y = op2(op1(a, b), c)                      written when y is not NULL
+ *     row_index[r] = arg{min,max}_j y[r, j]      when row_index (int64 [rows]) is not NULL;
+ *                                                row_op CTB_MIN or CTB_MAX
+ *     *d_sum = sum of all y, in float64          when d_sum (device) is not NULL
+ * Results equal ctorch's eager sequence on the same inputs: y = op2(op1(a, b), c) (two BinaryFn
+ * calls, src/ops/binary_ops_cpu.cpp:251-254) bit for bit, row_index = argmin/argmax(y, -1)
+ * (src/ops/reduction_ops_cpu.cpp:236-297: first index on ties, first NaN wins) bit for bit, and
+ * the sum to float64 rounding (its own fixed order, so run-to-run identical). The eager sequence
+ * reads y twice more; this reads a once and writes y once. */
+CTB_API int ctb_chain_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                           const ctb_view* y, int row_op, const ctb_view* row_index, double* d_sum,
+                           void* scratch, size_t scratch_bytes, ctb_stream stream);
+
 /* ---- sharded reductions (multi-GPU layer) ---- */
 
 /* Scratch bytes for ctb_sum_partial. */

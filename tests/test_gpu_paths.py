@@ -319,3 +319,64 @@ def test_front_door_errors(cuda_ok):
         cb.mean(a.int())
     assert cb.sum(torch.ones(3, 0, device="cuda"), [1]).tolist() == [0.0, 0.0, 0.0]
     assert torch.isnan(cb.mean(torch.ones(3, 0, device="cuda"), [1])).all()
+
+
+CHAIN_ROWS = [
+    # (rows, cols, dtype, row_op, b scalar?, special values?)
+    (4096, 8192, np.float32, "min", False, False),
+    (3000, 1001, np.float32, "max", False, True),
+    (777, 64, np.float64, "min", False, True),
+    (500, 130, np.float32, "min", True, True),
+    (1, 5, np.float32, "max", False, True),
+]
+
+
+@pytest.mark.parametrize("rows,cols,dt,row_op,scalar,special", CHAIN_ROWS)
+@pytest.mark.parametrize("ops", [("sub", "mul"), ("add", "div")])
+def test_chain_rows_single_pass(cuda_ok, oracle, rows, cols, dt, row_op, scalar, special, ops):
+    import torch
+
+    import ctorch_b200 as cb
+
+    rng = np.random.default_rng(_seed(rows, cols, row_op, ops))
+    x = rng.standard_normal((rows, cols)).astype(dt)
+    if special:
+        x = np.round(x * 2) / 2  # ties
+        x = x.astype(dt)
+        x.flat[::997] = np.nan
+        x[0, :] = np.inf if row_op == "min" else -np.inf  # a row of identities -> index 0
+        if rows > 2:
+            x[1, 3:] = np.inf
+            x[1, 2] = -np.inf
+    r = (rng.uniform(0.5, 2.0, () if scalar else (1, cols))).astype(dt)
+    tx, tr = torch.from_numpy(x).cuda(), torch.from_numpy(np.asarray(r)).cuda()
+    y, k, s = cb.chain_rows(ops[0], ops[1], tx, tr, tr, row_op=row_op)
+    ry = oracle.binary(ops[1], oracle.binary(ops[0], x, np.asarray(r)), np.asarray(r))
+    assert_bitexact(y.cpu().numpy(), ry, "chain_rows y", nan_payload=False)
+    assert_bitexact(k.cpu().numpy(), oracle.reduce_idx(row_op, ry, 1, values=False), "chain_rows index")
+    ref_sum = float(np.sum(ry.astype(np.float64)))
+    got = float(s.cpu().numpy()[0])
+    if np.isnan(ref_sum):
+        assert np.isnan(got)
+    elif np.isinf(ref_sum):
+        assert got == ref_sum
+    else:
+        assert abs(got - ref_sum) <= 1e-12 * max(1.0, abs(np.sum(np.abs(ry.astype(np.float64)))))
+    # without y / without the sum
+    _, k2, _ = cb.chain_rows(ops[0], ops[1], tx, tr, tr, row_op=row_op, write_y=False, want_sum=False)
+    assert torch.equal(k2, k)
+
+
+def test_sharded_step_fused_matches_three_kernel_step(cuda_ok):
+    import torch
+
+    from ctorch_b200.sharded import ShardedSum, sharded_step, sharded_step_fused
+    from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
+
+    x = device_fill(torch.empty((20000, 8192), device="cuda"), NORMAL, 4, 0, 0.0, 1.0)
+    r = device_fill(torch.empty((1, 8192), device="cuda"), UNIFORM, 4, 1, -1.0, 1.0)
+    y1, s1, k1 = sharded_step(x, r, ShardedSum(x.device, 1))
+    y2, s2, k2 = sharded_step_fused(x, r, ShardedSum(x.device, 1))
+    assert torch.equal(y1, y2)
+    assert torch.equal(k1, k2)
+    assert abs(float(s1) - float(s2)) <= 1e-6 * max(1.0, abs(float(s1)))
