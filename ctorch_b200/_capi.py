@@ -66,6 +66,7 @@ def _load() -> ctypes.CDLL:
         "ctb_unary": (i32, [i32, P, P, vp]),
         "ctb_reduce_scratch_bytes": (sz, [i32, P, P, u32]),
         "ctb_reduce": (i32, [i32, P, P, u32, vp, sz, vp]),
+        "ctb_reduce_noalloc": (i32, [i32, P, P, u32, vp]),
         "ctb_reduce_index_scratch_bytes": (sz, [P, i32]),
         "ctb_reduce_index": (i32, [i32, P, P, P, i32, vp, sz, vp]),
         "ctb_index_select": (i32, [P, i32, P, P, vp, vp]),

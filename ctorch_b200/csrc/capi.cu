@@ -33,6 +33,7 @@ int index_select_dispatch(const ctb_view* src, int dim, const ctb_view* idx, con
                           int32_t* status, cudaStream_t st);
 int fill_random(const ctb_view* out, int dist, uint64_t seed, uint64_t stream_id, int64_t first,
                 double lo, double hi, cudaStream_t st);
+int reduce_noalloc(int op, const ctb_view* in, const ctb_view* out, uint32_t mask, cudaStream_t st);
 size_t fused_rows_scratch(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
                           const ctb_view* y, int row_op, const ctb_view* idx);
 int fused_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
@@ -271,6 +272,15 @@ int ctb_reduce(int op, const ctb_view* in, const ctb_view* out, uint32_t mask, v
         if (op == CTB_MAX || op == CTB_MIN)
             return minmax_dispatch(op, in, out, nullptr, mask, scratch, scratch_bytes, st, nullptr);
         return sum_like_dispatch(op, in, out, mask, scratch, scratch_bytes, st, nullptr);
+    });
+}
+
+int ctb_reduce_noalloc(int op, const ctb_view* in, const ctb_view* out, uint32_t mask,
+                       ctb_stream stream) {
+    return guarded([&]() -> int {
+        t_error.clear();
+        if (int r = reduce_checks(op, in, out)) return r;
+        return reduce_noalloc(op, in, out, mask, static_cast<cudaStream_t>(stream));
     });
 }
 

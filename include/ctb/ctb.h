@@ -128,6 +128,21 @@ CTB_API size_t ctb_reduce_scratch_bytes(int op, const ctb_view* in, const ctb_vi
 CTB_API int ctb_reduce(int op, const ctb_view* in, const ctb_view* out, uint32_t reduce_mask,
                void* scratch, size_t scratch_bytes, ctb_stream stream);
 
+/* ctb_reduce without scratch from the caller, for callers that cannot allocate device memory:
+ * a plain C or FFI host with no device allocator of its own to hand out scratch, or a process
+ * that fixes its device memory at start-up and must not call cudaMalloc later (it can fail under
+ * fragmentation and it synchronises the device). Same arguments, results and errors as
+ * ctb_reduce; allocates nothing. Split reductions use a fixed 4 MiB array in the library's device
+ * image instead (every GPU that loads the library holds it until exit); a reduction that would
+ * need more returns CTB_ERR_SCRATCH and names the size. The first call on each device looks up
+ * the array's device address (with that device current) and caches it, so make that first call
+ * before any stream capture. All calls on a device share the one array and nothing in it needs
+ * clearing between calls, but calls that overlap on the GPU (two streams, or two host threads)
+ * race on it: serialise them. No counterpart in ctorch (ctorch's CUDA reductions always take
+ * scratch from its caching allocator). */
+CTB_API int ctb_reduce_noalloc(int op, const ctb_view* in, const ctb_view* out, uint32_t reduce_mask,
+                               ctb_stream stream);
+
 /* Scratch bytes ctb_reduce_index needs (0 when none). */
 CTB_API size_t ctb_reduce_index_scratch_bytes(const ctb_view* in, int axis);
 
