@@ -437,6 +437,167 @@ def run_case(args):
     return 0
 
 
+# ------------------------------------------------------------------------------- per-op suite
+
+def run_suite(args):
+    """Per-op device time and GB/s for every op of the five configurations, one JSON line per op.
+
+    Each op (or, for configuration 1, whose working set is about the size of L2, a round of the op
+    on 4 separate copies of its inputs) is captured in a CUDA graph and replayed `--steps` times
+    back to back between CUDA events on the replay stream; the op's time is the elapsed time per
+    call. The inputs touched between two calls on the same data exceed the 126 MB L2, so no flush
+    is needed, and no host (Python / ctypes) time falls inside the measurement. ctorch's own CPU
+    path (oracle/_ref, its public front-doors, one thread) is timed on the same inputs, or on a
+    stated sample of them, unless --no-cpu-baseline is given."""
+    import torch
+
+    import ctorch_b200 as cb
+    from ctorch_b200.sharded import ShardedSum
+    from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = measured_peak()
+    t = lambda shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
+    ref = None
+    if not args.no_cpu_baseline:
+        from oracle.oracle import ref as get_ref
+
+        ref = get_ref()
+
+    def graph_ms(fns):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                for fn in fns:
+                    fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for fn in fns:
+                fn()
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / (args.steps * len(fns))
+
+    def cpu_ms(fn, reps=1):
+        if ref is None:
+            return None
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps * 1e3
+
+    def emit(config, op, fn, nbytes, elems, cpu=None, cpu_elems=None, note=""):
+        ms = graph_ms(fn if isinstance(fn, list) else [fn])
+        line = {"config": config, "op": op, "ms": ms, "gbs": nbytes / ms / 1e6,
+                "frac_of_measured_peak": nbytes / ms / 1e6 / peak, "peak_gbs": peak,
+                "peak_kind": peak_kind, "algorithmic_bytes": nbytes, "elements_per_s": elems / ms * 1e3}
+        if cpu is not None and ref is not None:
+            cms = cpu_ms(cpu)
+            ce = cpu_elems or elems
+            line["cpu"] = {"ms": cms, "elements": ce, "elements_per_s": ce / cms * 1e3, "threads": 1,
+                           "speedup": (elems / ms) / (ce / cms)}
+        if note:
+            line["note"] = note
+        print(json.dumps(line), flush=True)
+
+    def rt(x):  # ctorch CPU tensor of a device tensor's values
+        return ref.tensor(x.cpu().numpy()) if ref is not None else None
+
+    # config 1: 4 copies of the inputs, used in turn (4 x 134 MB > L2)
+    a = device_fill(t((4096, 4096)), UNIFORM, 0, 0, -1.0, 1.0)
+    b = device_fill(t((1, 4096)), UNIFORM, 0, 1, -1.0, 1.0)
+    c = cb.add(a, b)
+    ra, rb, rc = rt(a), rt(b), rt(c)
+    copies = [(a.clone(), b.clone(), c.clone()) for _ in range(4)]
+    rot = "4 copies of the inputs used in turn (536 MB > L2)"
+    emit(1, "add", [lambda q=q: cb.add(q[0], q[1]) for q in copies], 134234112, 4096 * 4096,
+         lambda: ref.binary("add", ra, rb), note=rot)
+    emit(1, "relu", [lambda q=q: cb.relu(q[2]) for q in copies], 134217728, 4096 * 4096,
+         lambda: ref.unary("relu", rc), note=rot)
+    emit(1, "relu(add) one pass", [lambda q=q: cb.binary_unary("add", "relu", q[0], q[1]) for q in copies],
+         134234112, 4096 * 4096, lambda: ref.unary("relu", ref.binary("add", ra, rb)), note=rot)
+    del a, b, c, ra, rb, rc, copies
+    # config 2
+    x = device_fill(t((8192, 8192)), NORMAL, 1, 0, 0.0, 1.0)
+    u = device_fill(t((8192, 8192)), UNIFORM, 1, 1, -1.0, 1.0)
+    xp = cb.add(cb.mul(u, torch.tensor(0.001, device=dev)), torch.tensor(1.0, device=dev))
+    del u
+    rx, rxp = rt(x), rt(xp)
+    rd = 268435456
+    emit(2, "sum dim=1 keepdim", lambda: cb.sum(x, [1], True), rd + 32768, 8192 * 8192,
+         lambda: ref.reduce("sum", rx, [1], True))
+    emit(2, "mean dim=1 keepdim", lambda: cb.mean(x, [1], True), rd + 32768, 8192 * 8192,
+         lambda: ref.reduce("mean", rx, [1], True))
+    emit(2, "max dim=0 (values+indices)", lambda: cb.max(x, 0, False), rd + 32768 + 65536, 8192 * 8192,
+         lambda: ref.reduce_idx("max", rx, 0))
+    emit(2, "argmax dim=0", lambda: cb.argmax(x, 0, False), rd + 65536, 8192 * 8192,
+         lambda: ref.arg("argmax", rx, 0))
+    emit(2, "prod dim=1", lambda: cb.prod(xp, [1], False), rd + 32768, 8192 * 8192,
+         lambda: ref.reduce("prod", rxp, [1], False))
+    del x, xp, rx, rxp
+    torch.cuda.empty_cache()
+    # config 3 (the CPU leg gathers a 1/16 sample of the indices)
+    idx = device_fill(t((4_194_304,), torch.int64), UNIFORM, 2, 2, 0, 999_999)
+    for dt, name in ((torch.float32, "float32"), (torch.int32, "int32")):
+        if dt == torch.float32:
+            tab = device_fill(t((1_000_000, 256)), NORMAL, 2, 0, 0.0, 1.0)
+        else:
+            tab = device_fill(t((1_000_000, 256), torch.int32), UNIFORM, 2, 1, -(2**30), 2**30 - 1)
+        rtab = rt(tab)
+        ridx = ref.tensor(idx[:262144].cpu().numpy()) if ref is not None else None
+        emit(3, f"index_select {name}", lambda: cb.index_select_async(tab, 0, idx), 8623489024,
+             4_194_304 * 256, lambda: ref.index_select(rtab, 0, ridx), 262144 * 256,
+             note="CPU leg: the first 262144 of the 4194304 indices")
+        del tab, rtab
+        torch.cuda.empty_cache()
+    del idx
+    # config 4
+    i4 = device_fill(t((64, 512, 1024), torch.int32), UNIFORM, 3, 0, -1000, 1000)
+    f4 = device_fill(t((64, 1024, 512)), UNIFORM, 3, 1, -1.0, 1.0)
+    d4 = device_fill(t((1, 512, 1), torch.float64), UNIFORM, 3, 2, 0.5, 2.0)
+    p4 = cb.mul(i4, f4.permute(0, 2, 1))
+    ri, rf, rdd, rp = rt(i4), rt(f4), rt(d4), rt(p4)
+    rft = rf.permute([0, 2, 1]) if ref is not None else None
+    emit(4, "mul int32 x float32^T -> float32", lambda: cb.mul(i4, f4.permute(0, 2, 1)), 402653184,
+         64 * 512 * 1024, lambda: ref.binary("mul", ri, rft),
+         note="CPU leg: ctorch's front-door casts the int32 operand on the host first")
+    emit(4, "div float32 / float64[1,512,1] -> float64", lambda: cb.div(p4, d4), 402657280,
+         64 * 512 * 1024, lambda: ref.binary("div", rp, rdd))
+    del i4, f4, d4, p4, ri, rf, rdd, rp, rft
+    torch.cuda.empty_cache()
+    # config 5, one GPU, the kernels of the step (the CPU leg runs on 32768 of the 262144 rows)
+    x5 = device_fill(t((ROWS, COLS)), NORMAL, SEED, 0, 0.0, 1.0)
+    r5 = device_fill(t((1, COLS)), UNIFORM, SEED, 1, -1.0, 1.0)
+    y5 = cb.binary_chain("sub", "mul", x5, r5, r5)
+    summer = ShardedSum(dev, 1)
+    xs = ref.tensor(x5[:32768].cpu().numpy()) if ref is not None else None
+    rr = rt(r5)
+    ys = ref.binary("mul", ref.binary("sub", xs, rr), rr) if ref is not None else None
+    n5 = ROWS * COLS
+    emit(5, "sub (eager)", lambda: cb.sub(x5, r5), n5 * 8 + COLS * 4, n5, lambda: ref.binary("sub", xs, rr), 32768 * COLS)
+    emit(5, "(X-r)*r one pass", lambda: cb.binary_chain("sub", "mul", x5, r5, r5), n5 * 8 + COLS * 4, n5,
+         lambda: ref.binary("mul", ref.binary("sub", xs, rr), rr), 32768 * COLS)
+    emit(5, "sum whole (float64 partial)", lambda: summer(y5), n5 * 4, n5, lambda: ref.reduce("sum", ys), 32768 * COLS)
+    emit(5, "argmin dim=1", lambda: cb.argmin(y5, 1), n5 * 4 + ROWS * 8, n5, lambda: ref.arg("argmin", ys, 1), 32768 * COLS)
+    emit(5, "chain + row argmin + sum, one pass", lambda: cb.chain_rows("sub", "mul", x5, r5, r5, out_sum=summer.partial),
+         n5 * 8 + COLS * 4 + ROWS * 8, n5, lambda: (ref.reduce("sum", ys), ref.arg("argmin", ys, 1)), 32768 * COLS,
+         note="CPU leg: sum and argmin of the precomputed Y sample")
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -450,9 +611,13 @@ def main():
                     help="profiling mode: launch one kernel (chain_rows, chain, sub, sum, argmin, add, relu, sum_rows, "
                          "prod_rows, argmax_cols, max_cols, index_select, mul_t, div_b) --warmup + --steps times")
     ap.add_argument("--rows", type=int, default=16384, help="rows of X for --case (default 16384: 512 MiB)")
+    ap.add_argument("--suite", action="store_true",
+                    help="per-op device time, GB/s and ctorch CPU time for every op of the five configurations")
     args = ap.parse_args()
     if args.case:
         return run_case(args)
+    if args.suite:
+        return run_suite(args)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":

@@ -16,6 +16,7 @@ from .ops import (  # noqa: F401
     argmax,
     argmin,
     binary_chain,
+    binary_unary,
     chain_rows,
     broadcast_shape,
     div,

@@ -20,6 +20,8 @@ extern template int binary_dispatch<CTB_SUB>(const ctb_view*, const ctb_view*, c
 extern template int binary_dispatch<CTB_MUL>(const ctb_view*, const ctb_view*, const ctb_view*, cudaStream_t);
 extern template int binary_dispatch<CTB_DIV>(const ctb_view*, const ctb_view*, const ctb_view*, cudaStream_t);
 int unary_dispatch(int op, const ctb_view* in, const ctb_view* out, cudaStream_t st);
+int bin_unary_dispatch(int op, int uop, const ctb_view* a, const ctb_view* b, const ctb_view* out,
+                       cudaStream_t st);
 int chain_dispatch(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
                    const ctb_view* out, cudaStream_t st);
 int sum_like_dispatch(int op, const ctb_view* in, const ctb_view* out, uint32_t mask, void* scratch,
@@ -215,6 +217,24 @@ int ctb_binary_chain(int op1, int op2, const ctb_view* a, const ctb_view* b, con
             c->dtype != dt || mid_dtype != dt)
             return fail(CTB_ERR_DTYPE, "fused chains take float32 or float64 operands of one dtype");
         return chain_dispatch(op1, op2, a, b, c, out, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int ctb_binary_unary(int op, int unary_op, const ctb_view* a, const ctb_view* b, const ctb_view* out,
+                     ctb_stream stream) {
+    return guarded([&]() -> int {
+        t_error.clear();
+        if (int rc = check_views({a, b, out})) return rc;
+        if (op < CTB_ADD || op > CTB_DIV) return fail(CTB_ERR_ARGUMENT, "unknown binary op");
+        if (unary_op != CTB_RELU && unary_op != CTB_NEG && unary_op != CTB_ABS)
+            return fail(CTB_ERR_ARGUMENT, "the fused unary op must be relu, neg or abs");
+        const int dt = out->dtype;
+        if (a->dtype != dt || b->dtype != dt ||
+            (dt != CTB_FLOAT32 && dt != CTB_FLOAT64 && dt != CTB_INT32 && dt != CTB_INT64))
+            return fail(CTB_ERR_DTYPE, "binary+unary chains take int32/int64/float32/float64 operands of one dtype");
+        if (op == CTB_DIV && (dt == CTB_INT32 || dt == CTB_INT64))
+            return fail(CTB_ERR_DTYPE, "integer division is not supported; cast operands to float32/float64 first");
+        return bin_unary_dispatch(op, unary_op, a, b, out, static_cast<cudaStream_t>(stream));
     });
 }
 

@@ -1,11 +1,12 @@
 // elementwise.cuh — sm_100a elementwise kernels (binary, unary, fused binary chains).
 //
 // One functor `Fn` computes an output element from up to three input elements (each in its own
-// storage type; Fn converts). The planner (plan.cu) picks one of five launch shapes:
+// storage type; Fn converts). The planner (plan.cu) picks one of six launch shapes:
 //   Flat      rank 1 after collapsing, unit/zero strides: grid-stride 16-byte packs, 4 in flight
-//   RowsLong  unit/zero inner strides, rows >= 128 packs: CTA tiles of 1024 packs along a row,
-//             the row's base offsets decoded once per tile (FastDiv, no 64-bit divides)
-//   RowsShort same, short rows: each pack decodes its own row
+//   RowsLong  unit/zero inner strides, rows >= 1024 packs: CTA tiles of 1024 or 2048 packs along a
+//             row, the row's base offsets decoded once per tile (FastDiv, no 64-bit divides)
+//   RowsMid   same, rows of 128..1023 packs: warp tiles of 128 packs, decoded once per tile
+//   RowsShort same, shorter rows: each pack decodes its own row
 //   Tiled     one input read transposed (unit stride on an outer dim): 64x64 tile staged through
 //             shared memory so both the transposed read and the output write are coalesced
 //   General   anything else: per-element coordinate decode
@@ -21,6 +22,10 @@ namespace ctb {
 constexpr int kEwBlock = 256;
 constexpr int kEwUnroll = 4;
 constexpr int kTile = 64;
+// Resident CTAs asked of the register allocator for division by a per-row scalar: at 4 (64
+// registers) the reciprocal sequence of four packs a thread no longer overlaps its loads, and the
+// kernel runs about 40% slower on float32[64,512,1024] / float64[1,512,1].
+constexpr int kRowDivMinBlocks = 3;
 
 struct NoIn {};
 
@@ -50,6 +55,91 @@ __device__ __forceinline__ void ew_decode_row(const EwArgs& p, uint64_t row, int
         row = q;
     }
 }
+
+// Division by a divisor that is constant along a row, from its correctly rounded reciprocal
+// y = RN(1/b), computed once per row:
+//   q0 = RN(a*y)                   within about 2 ulp of a/b
+//   q1 = RN(q0 + RN(a - b*q0)*y)   faithful (one of the two neighbours of a/b)
+//   q2 = RN(q1 + (a - b*q1)*y)     = RN(a/b)
+// a - b*q1 is exact in an FMA because q1 is faithful, and the last step is Markstein's theorem
+// (P. Markstein, IBM J. Res. Dev. 34(1), 1990): with y within half an ulp of 1/b and q1 faithful,
+// q1 + r*y cannot land on the other side of a rounding midpoint from a/b. The theorem assumes no
+// overflow, underflow or subnormal along the way, so the sequence only runs when a, b and the
+// quotient have exponents at least `kMargin` away from both ends of the range; zeros,
+// infinities, NaNs, subnormals and extreme magnitudes take the IEEE division. Either way the
+// result is the correctly rounded quotient, bit-identical to a / b.
+template <class T> struct FpTraits;
+template <> struct FpTraits<double> {
+    static constexpr int kMax = 2046, kMargin = 64, kBias = 1023;
+};
+template <> struct FpTraits<float> {
+    static constexpr int kMax = 254, kMargin = 32, kBias = 127;
+};
+
+template <class T> __device__ __forceinline__ int fp_exponent(T x) {
+    if constexpr (std::is_same_v<T, double>)
+        return static_cast<int>((static_cast<unsigned>(__double2hiint(x)) >> 20) & 0x7ff);
+    else
+        return static_cast<int>((__float_as_uint(x) >> 23) & 0xff);
+}
+
+// The per-row state: the divisor, its reciprocal, and the range [lo, lo + span] of dividend
+// exponents for which the sequence runs. A divisor that is itself out of range gets lo = 2^30,
+// span = 0, a range no exponent (0..2047) falls in.
+template <class T> struct RowDivisor {
+    T b, y;
+    int lo;
+    unsigned span;
+};
+
+template <class T> __device__ __forceinline__ RowDivisor<T> row_divisor(T b) {
+    using F = FpTraits<T>;
+    RowDivisor<T> d;
+    d.b = b;
+    const int eb = fp_exponent(b);
+    // quotient exponent ea - eb + bias must also stay in [margin, max - margin]
+    const int lo = max(F::kMargin, eb - F::kBias + F::kMargin);
+    const int hi = min(F::kMax - F::kMargin, eb - F::kBias + F::kMax - F::kMargin);
+    const bool ok = eb >= F::kMargin && eb <= F::kMax - F::kMargin && hi >= lo;
+    d.lo = ok ? lo : (1 << 30);
+    d.span = ok ? static_cast<unsigned>(hi - lo) : 0u;
+    if constexpr (std::is_same_v<T, double>) d.y = ok ? __drcp_rn(b) : 0.0;
+    else d.y = ok ? __frcp_rn(b) : 0.0f;
+    return d;
+}
+
+template <class T> __device__ __forceinline__ T div_by_row(T a, const RowDivisor<T>& d) {
+    if (static_cast<unsigned>(fp_exponent(a) - d.lo) <= d.span) {
+        if constexpr (std::is_same_v<T, double>) {
+            const double q0 = __dmul_rn(a, d.y);
+            const double q1 = __fma_rn(__fma_rn(-d.b, q0, a), d.y, q0);
+            return __fma_rn(__fma_rn(-d.b, q1, a), d.y, q1);
+        } else {
+            const float q0 = __fmul_rn(a, d.y);
+            const float q1 = __fmaf_rn(__fmaf_rn(-d.b, q0, a), d.y, q0);
+            return __fmaf_rn(__fmaf_rn(-d.b, q1, a), d.y, q1);
+        }
+    }
+    return BinOp<CTB_DIV>::template apply<T>(a, d.b);
+}
+
+// kWideRows: cheap enough per element for the wide row tiles (see ew_rows_long); division is not.
+template <int OP, class O> struct FnBinary {
+    static constexpr bool kWideRows = OP != CTB_DIV;
+    template <class A, class B> __device__ __forceinline__ O operator()(A a, B b) const {
+        return BinOp<OP>::template apply<O>(cvt<O>(a), cvt<O>(b));
+    }
+};
+
+// Row kernels whose second operand is a per-row scalar check RowPrep<Fn>::kActive: when it is set
+// (float and double division) they prepare the scalar once per row with row_divisor and divide each
+// element of the row with div_by_row; every other functor is applied as it is.
+template <class Fn> struct RowPrep {
+    static constexpr bool kActive = false;
+};
+template <class O> struct RowPrep<FnBinary<CTB_DIV, O>> {
+    static constexpr bool kActive = is_float_v<O>;
+};
 
 // ------------------------------------------------------------------------------------------------
 template <class Fn, class O, class I0, class I1, class I2, int NIN>
@@ -124,11 +214,10 @@ __device__ __forceinline__ void inner_bcast(const EwArgs& p, bool& b0, bool& b1,
     }
 }
 
-template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK>
+template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK, int U = kEwUnroll>
 __device__ __forceinline__ void ew_row_segment(const EwArgs& p, const Fn& fn, const int64_t* off,
                                                int64_t c0, int64_t cstep, int count) {
     constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
-    constexpr int U = kEwUnroll;
     O* __restrict__ out = static_cast<O*>(p.out) + off[0];
     const I0* __restrict__ in0 = static_cast<const I0*>(p.in[0]) + off[1];
     const I1* __restrict__ in1 = static_cast<const I1*>(p.in[1]) + off[2];
@@ -152,23 +241,37 @@ __device__ __forceinline__ void ew_row_segment(const EwArgs& p, const Fn& fn, co
             if constexpr (NIN > 2) if (!b2) x2[u] = load_pack<I2, V>(in2 + c * V);
         }
     }
+    if constexpr (BMASK == 2 && NIN == 2 && RowPrep<Fn>::kActive) {
+        const RowDivisor<O> d = row_divisor<O>(cvt<O>(s1));
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-        const int64_t c = c0 + u * cstep;
-        if (u < count && c < p.vpr) {
-            Pack<O, V> o;
+        for (int u = 0; u < U; ++u) {
+            const int64_t c = c0 + u * cstep;
+            if (u < count && c < p.vpr) {
+                Pack<O, V> o;
 #pragma unroll
-            for (int e = 0; e < V; ++e)
-                o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, b0 ? s0 : x0[u].v[e],
-                                                          b1 ? s1 : x1[u].v[e],
-                                                          b2 ? s2 : x2[u].v[e]);
-            store_pack<O, V>(out + c * V, o);
+                for (int e = 0; e < V; ++e) o.v[e] = div_by_row<O>(cvt<O>(x0[u].v[e]), d);
+                store_pack<O, V>(out + c * V, o);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t c = c0 + u * cstep;
+            if (u < count && c < p.vpr) {
+                Pack<O, V> o;
+#pragma unroll
+                for (int e = 0; e < V; ++e)
+                    o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, b0 ? s0 : x0[u].v[e],
+                                                              b1 ? s1 : x1[u].v[e],
+                                                              b2 ? s2 : x2[u].v[e]);
+                store_pack<O, V>(out + c * V, o);
+            }
         }
     }
 }
 
 // Min resident CTAs to ask of the register allocator: 4 when the packs live across the load
-// latency are small (<= 48 bytes per thread-pack), else 2.
+// latency are small (<= 48 bytes per thread-pack; 3 with three inputs), else 2.
 template <class O, class I0, class I1, class I2, int NIN, int BMASK> constexpr int rows_min_blocks() {
     constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
     if (BMASK < 0) return 2;
@@ -176,27 +279,50 @@ template <class O, class I0, class I1, class I2, int NIN, int BMASK> constexpr i
     if (!(BMASK & 1)) bytes += V * static_cast<int>(sizeof(I0));
     if (NIN > 1 && !(BMASK & 2)) bytes += V * static_cast<int>(sizeof(I1));
     if (NIN > 2 && !(BMASK & 4)) bytes += V * static_cast<int>(sizeof(I2));
+    // three inputs with one of them a per-row scalar still carry a scalar per pack in flight
+    if (NIN > 2 && bytes <= 48) return 3;
     return bytes <= 48 ? 4 : 2;
 }
 
-template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK>
-__global__ void __launch_bounds__(kEwBlock, (rows_min_blocks<O, I0, I1, I2, NIN, BMASK>()))
-    ew_rows_long(EwArgs p, Fn fn) {
-    const int64_t seg = static_cast<int64_t>(kEwBlock) * kEwUnroll;
+// Rows of at least kRowsLongPacks packs: CTA tiles of kEwBlock x U packs along one row, the row's
+// base offsets decoded once per tile; p.aux holds the tiles per row for that U. The launcher
+// takes U = 4, or 8 with half the resident CTAs on rows of 2048 packs or more (one tile covers a
+// whole 8192-float row: about 5% faster there than two tiles of 4 packs a thread).
+template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK, int U, int MINB>
+__global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_long(EwArgs p, Fn fn) {
+    const int64_t seg = static_cast<int64_t>(kEwBlock) * U;
     const int64_t tiles = p.rows * static_cast<int64_t>(p.aux.d);
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
         uint64_t row, s;
         p.aux.divmod(static_cast<uint64_t>(t), row, s);
         int64_t off[kMaxOps];
         ew_decode_row(p, row, NIN + 1, off);
-        ew_row_segment<Fn, O, I0, I1, I2, NIN, BMASK>(p, fn, off, static_cast<int64_t>(s) * seg + threadIdx.x,
-                                                      kEwBlock, kEwUnroll);
+        ew_row_segment<Fn, O, I0, I1, I2, NIN, BMASK, U>(p, fn, off, static_cast<int64_t>(s) * seg + threadIdx.x,
+                                                         kEwBlock, U);
     }
 }
 
-template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK>
-__global__ void __launch_bounds__(kEwBlock, (rows_min_blocks<O, I0, I1, I2, NIN, BMASK>()))
-    ew_rows_short(EwArgs p, Fn fn) {
+// Rows of kRowsMidPacks up to kRowsLongPacks packs: each warp takes tiles of 32 x U packs along
+// one row, so the row's base offsets (and a per-row divisor) are worked out once per tile rather
+// than per pack. p.aux holds the tiles per row for that U.
+template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK, int U, int MINB>
+__global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_mid(EwArgs p, Fn fn) {
+    constexpr int kWarps = kEwBlock / 32;
+    const int64_t seg = 32 * U;
+    const int64_t tiles = p.rows * static_cast<int64_t>(p.aux.d);
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * kWarps;
+    const int lane = threadIdx.x & 31;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles; t += nw) {
+        uint64_t row, s;
+        p.aux.divmod(static_cast<uint64_t>(t), row, s);
+        int64_t off[kMaxOps];
+        ew_decode_row(p, row, NIN + 1, off);
+        ew_row_segment<Fn, O, I0, I1, I2, NIN, BMASK, U>(p, fn, off, static_cast<int64_t>(s) * seg + lane, 32, U);
+    }
+}
+
+template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK, int MINB>
+__global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_short(EwArgs p, Fn fn) {
     constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
     constexpr int U = kEwUnroll;
     bool b0, b1, b2;
@@ -243,11 +369,17 @@ __global__ void __launch_bounds__(kEwBlock, (rows_min_blocks<O, I0, I1, I2, NIN,
         for (int u = 0; u < U; ++u) {
             if (oo[u] >= 0) {
                 Pack<O, V> o;
+                if constexpr (BMASK == 2 && NIN == 2 && RowPrep<Fn>::kActive) {
+                    const RowDivisor<O> d = row_divisor<O>(cvt<O>(s1[u]));
 #pragma unroll
-                for (int e = 0; e < V; ++e)
-                    o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, b0 ? s0[u] : x0[u].v[e],
-                                                              b1 ? s1[u] : x1[u].v[e],
-                                                              b2 ? s2[u] : x2[u].v[e]);
+                    for (int e = 0; e < V; ++e) o.v[e] = div_by_row<O>(cvt<O>(x0[u].v[e]), d);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < V; ++e)
+                        o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, b0 ? s0[u] : x0[u].v[e],
+                                                                  b1 ? s1[u] : x1[u].v[e],
+                                                                  b2 ? s2[u] : x2[u].v[e]);
+                }
                 store_pack<O, V>(out + oo[u], o);
             }
         }
@@ -501,38 +633,89 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
         break;
     }
     case EwPath::RowsLong: {
-        const int64_t tiles = a.rows * static_cast<int64_t>(a.aux.d);
-#define CTB_RL(M)                                                        \
+        // wide tiles only for 4-byte types throughout (mixed widths double the registers a pack
+        // takes, and 8-byte types spill at 8 packs a thread)
+        constexpr bool kWide = Fn::kWideRows && sizeof(O) == 4 && sizeof(I0) == 4 &&
+                               (NIN < 2 || sizeof(I1) == 4) && (NIN < 3 || sizeof(I2) == 4);
+        const bool wide = kWide && a.vpr >= 2 * kRowsLongPacks;
+        EwArgs al = a;
+        const int64_t seg = static_cast<int64_t>(kEwBlock) * (wide ? 8 : 4);
+        al.aux = FastDiv(static_cast<uint64_t>((a.vpr + seg - 1) / seg));
+        const int64_t tiles = a.rows * static_cast<int64_t>(al.aux.d);
+#define CTB_RL(M, U, B)                                                  \
     {                                                                    \
-        auto k = &ew_rows_long<Fn, O, I0, I1, I2, NIN, M>;               \
-        k<<<wave_grid(k, tiles), kEwBlock, 0, st>>>(a, fn);              \
+        auto k = &ew_rows_long<Fn, O, I0, I1, I2, NIN, M, U, B>;         \
+        k<<<wave_grid(k, tiles), kEwBlock, 0, st>>>(al, fn);             \
+    }
+#define CTB_RL2(M)                                                       \
+    if constexpr (kWide) {                                               \
+        if (wide) CTB_RL(M, 8, 2)                                        \
+        else CTB_RL(M, 4, (rows_min_blocks<O, I0, I1, I2, NIN, M>()))    \
+    } else {                                                             \
+        CTB_RL(M, 4, (rows_min_blocks<O, I0, I1, I2, NIN, M>()))         \
     }
         switch (inner_mask(a, NIN)) {
-        case 0: CTB_RL(0) break;
-        case 1: CTB_RL(1) break;
+        case 0: CTB_RL2(0) break;
+        case 1: CTB_RL2(1) break;
         case 2:
-            if constexpr (NIN > 1) { CTB_RL(2) break; }
+            if constexpr (NIN > 1) {
+                // division by a per-row scalar: tiles of 4 packs a thread at kRowDivMinBlocks
+                if constexpr (RowPrep<Fn>::kActive) {
+                    CTB_RL(2, 4, kRowDivMinBlocks)
+                } else {
+                    CTB_RL2(2)
+                }
+                break;
+            }
             [[fallthrough]];
-        default: CTB_RL(-1) break;
+        default: CTB_RL(-1, 4, 2) break;
         }
+#undef CTB_RL2
 #undef CTB_RL
+        break;
+    }
+    case EwPath::RowsMid: {
+        const int64_t tiles = a.rows * static_cast<int64_t>(a.aux.d);
+        const int64_t work = (tiles + kEwBlock / 32 - 1) / (kEwBlock / 32);
+#define CTB_RM(M, B)                                                                             \
+    {                                                                                            \
+        auto k = &ew_rows_mid<Fn, O, I0, I1, I2, NIN, M, kRowsMidUnroll, B>;                     \
+        k<<<wave_grid(k, work), kEwBlock, 0, st>>>(a, fn);                                       \
+    }
+        switch (inner_mask(a, NIN)) {
+        case 0: CTB_RM(0, (rows_min_blocks<O, I0, I1, I2, NIN, 0>())) break;
+        case 1: CTB_RM(1, (rows_min_blocks<O, I0, I1, I2, NIN, 1>())) break;
+        case 2:
+            if constexpr (NIN > 1) {
+                if constexpr (RowPrep<Fn>::kActive) CTB_RM(2, kRowDivMinBlocks)
+                else CTB_RM(2, (rows_min_blocks<O, I0, I1, I2, NIN, 2>()))
+                break;
+            }
+            [[fallthrough]];
+        default: CTB_RM(-1, 2) break;
+        }
+#undef CTB_RM
         break;
     }
     case EwPath::RowsShort: {
         const int64_t nvec = a.rows * a.vpr;
         const int64_t work = (nvec + kEwBlock * kEwUnroll - 1) / (kEwBlock * kEwUnroll);
-#define CTB_RS(M)                                                        \
+#define CTB_RS(M, B)                                                     \
     {                                                                    \
-        auto k = &ew_rows_short<Fn, O, I0, I1, I2, NIN, M>;              \
+        auto k = &ew_rows_short<Fn, O, I0, I1, I2, NIN, M, B>;           \
         k<<<wave_grid(k, work), kEwBlock, 0, st>>>(a, fn);               \
     }
         switch (inner_mask(a, NIN)) {
-        case 0: CTB_RS(0) break;
-        case 1: CTB_RS(1) break;
+        case 0: CTB_RS(0, (rows_min_blocks<O, I0, I1, I2, NIN, 0>())) break;
+        case 1: CTB_RS(1, (rows_min_blocks<O, I0, I1, I2, NIN, 1>())) break;
         case 2:
-            if constexpr (NIN > 1) { CTB_RS(2) break; }
+            if constexpr (NIN > 1) {
+                if constexpr (RowPrep<Fn>::kActive) CTB_RS(2, kRowDivMinBlocks)
+                else CTB_RS(2, (rows_min_blocks<O, I0, I1, I2, NIN, 2>()))
+                break;
+            }
             [[fallthrough]];
-        default: CTB_RS(-1) break;
+        default: CTB_RS(-1, 2) break;
         }
 #undef CTB_RS
         break;
@@ -569,16 +752,9 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// Functors
-
-template <int OP, class O> struct FnBinary {
-    template <class A, class B> __device__ __forceinline__ O operator()(A a, B b) const {
-        return BinOp<OP>::template apply<O>(cvt<O>(a), cvt<O>(b));
-    }
-};
-
 // op2(op1(a, b) rounded to M, c) rounded to O.
 template <int OP1, int OP2, class M, class O> struct FnChain {
+    static constexpr bool kWideRows = OP1 != CTB_DIV && OP2 != CTB_DIV;
     template <class A, class B, class C> __device__ __forceinline__ O operator()(A a, B b, C c) const {
         const M m = BinOp<OP1>::template apply<M>(cvt<M>(a), cvt<M>(b));
         return BinOp<OP2>::template apply<O>(cvt<O>(m), cvt<O>(c));

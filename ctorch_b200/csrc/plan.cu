@@ -12,6 +12,7 @@ const char* ew_path_name(EwPath p) {
     case EwPath::Flat: return "flat";
     case EwPath::RowsLong: return "rows_long";
     case EwPath::RowsShort: return "rows_short";
+    case EwPath::RowsMid: return "rows_mid";
     case EwPath::Tiled: return "tiled";
     case EwPath::General: return "general";
     }
@@ -176,11 +177,12 @@ int plan_elementwise(const ctb_view* out, const ctb_view* const* ins, int nin, c
     }
     if (inner_ok && aligned && a.L % vec == 0) {
         a.vpr = a.L / vec;
-        constexpr int kBlock = 256, kUnroll = 4;
-        if (a.vpr >= kBlock * kUnroll) {
-            const int64_t seg = static_cast<int64_t>(kBlock) * kUnroll;
-            a.aux = FastDiv(static_cast<uint64_t>((a.vpr + seg - 1) / seg));
+        if (a.vpr >= kRowsLongPacks) {
+            a.aux = FastDiv(static_cast<uint64_t>((a.vpr + kRowsLongPacks - 1) / kRowsLongPacks));
             plan.path = EwPath::RowsLong;
+        } else if (a.vpr >= kRowsMidPacks) {
+            a.aux = FastDiv(static_cast<uint64_t>((a.vpr + kRowsMidPacks - 1) / kRowsMidPacks));
+            plan.path = EwPath::RowsMid;
         } else {
             a.aux = FastDiv(static_cast<uint64_t>(a.vpr));
             plan.path = EwPath::RowsShort;
@@ -366,6 +368,24 @@ int plan_reduction(const ctb_view* in, const ctb_view* out, const ctb_view* out2
     return CTB_OK;
 }
 
+// Split count in [1, max_split] whose CTAs (tiles * split) fill one or two whole waves of `slots`
+// best; a larger split must fill at least 2% more to be chosen (it costs partial-state traffic).
+static int64_t best_split(int64_t tiles, int64_t slots, int64_t max_split) {
+    int64_t best = 1;
+    double best_fill = -1.0;
+    const int64_t hi = std::max<int64_t>(1, std::min<int64_t>(max_split, 2 * slots / std::max<int64_t>(1, tiles)));
+    for (int64_t s = 1; s <= hi; ++s) {
+        const int64_t ctas = tiles * s;
+        const int64_t waves = (ctas + slots - 1) / slots;
+        const double fill = static_cast<double>(ctas) / static_cast<double>(waves * slots);
+        if (fill > best_fill + 0.02) {
+            best_fill = fill;
+            best = s;
+        }
+    }
+    return best;
+}
+
 size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int outer_vec,
                              const RedOcc& occ) {
     RedArgs& a = plan.args;
@@ -416,11 +436,12 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
         const int64_t tiles = tiles_n * batch;
         const int64_t slots = sms * occ.outer;
         int64_t split = 1;
-        if (tiles < slots) {
-            split = slots / tiles;
-            split = std::min<int64_t>(split, std::max<int64_t>(1, a.K / 64));
-            split = std::max<int64_t>(split, 1);
-        }
+        // partials are kept to 2 MiB: at most a few percent of the bytes the reduction reads
+        const int64_t cap = std::max<int64_t>(1, (int64_t(2) << 20) / std::max<int64_t>(1, a.kept * state_bytes));
+        if (tiles < 2 * slots) split = best_split(tiles, slots, std::max<int64_t>(1, std::min(a.K / 64, cap)));
+        // the kernel folds positions as 32-bit offsets within a chunk
+        constexpr int64_t kMaxChunk = (int64_t(1) << 31) - 2;
+        split = std::max<int64_t>(split, (a.K + kMaxChunk - 1) / kMaxChunk);
         int64_t chunk = (a.K + split - 1) / split;
         split = (a.K + chunk - 1) / chunk;
         a.split = static_cast<int>(split);

@@ -12,7 +12,15 @@ namespace ctb {
 // Elementwise iteration space over up to 4 operands (0 = out, 1..3 = inputs).
 constexpr int kMaxOps = 4;
 
-enum class EwPath : int { Empty = 0, Flat = 1, RowsLong = 2, RowsShort = 3, Tiled = 4, General = 5 };
+enum class EwPath : int { Empty = 0, Flat = 1, RowsLong = 2, RowsShort = 3, Tiled = 4, General = 5, RowsMid = 6 };
+
+// Row tiles (16-byte packs): RowsLong CTAs of 256 threads take 4 packs a thread along a row (8 on
+// rows of 2048 packs or more); RowsMid warps take kRowsMidUnroll packs a lane. Rows of at least
+// kRowsLongPacks go to RowsLong, rows of at least one warp tile to RowsMid, shorter ones to
+// RowsShort.
+constexpr int kRowsMidUnroll = 4;
+constexpr int64_t kRowsLongPacks = 1024;
+constexpr int64_t kRowsMidPacks = 32 * kRowsMidUnroll;
 
 struct EwSpace {
     int nops = 0;  // out + inputs
@@ -47,11 +55,11 @@ struct EwArgs {
     int64_t n;                     // total elements
     int64_t L;                     // innermost extent
     int64_t rows;                  // n / L
-    int64_t vpr;                   // vectors per row (RowsLong/RowsShort)
+    int64_t vpr;                   // vectors per row (RowsLong/RowsMid/RowsShort)
     int64_t shape[kMaxDims];
     int64_t stride[kMaxOps][kMaxDims];
     FastDiv div[kMaxDims];         // divisors = shape[d]
-    FastDiv aux;                   // RowsLong: segments per row; RowsShort: vectors per row;
+    FastDiv aux;                   // RowsLong (set by the launcher)/RowsMid: tiles per row; RowsShort: vectors per row;
                                    // Tiled: tiles along L
     FastDiv aux2;                  // Tiled: tiles along P
 };

@@ -28,7 +28,12 @@
 namespace ctb {
 
 constexpr int kRedBlock = 256;
-constexpr int kRedUnroll = 4;
+constexpr int kOuterBlock = 128;  // column strips: 4 warps, so twice the resident CTAs to spread over
+
+// Packs each thread keeps in flight (R::kUnroll): sums and products of 4-byte elements keep 8
+// (a warp has 4 KiB of loads outstanding per step); max/min states carry a position as well, so
+// they keep 4 to stay at 4 resident CTAs per SM.
+template <class R> constexpr int red_unroll() { return R::kUnroll; }
 
 // ------------------------------------------------------------------------------------------------
 // shuffles
@@ -55,6 +60,7 @@ template <class T, bool IsProd> struct RAccum {
     using In = T;
     using State = std::conditional_t<is_float_v<T>, double, uint64_t>;
     using Out = std::conditional_t<is_float_v<T>, T, int64_t>;
+    static constexpr int kUnroll = sizeof(T) <= 4 ? 8 : 4;
     __device__ __forceinline__ static State init() { return IsProd ? State(1) : State(0); }
     __device__ __forceinline__ static State conv(T v) {
         if constexpr (is_float_v<T>) return static_cast<double>(v);
@@ -66,6 +72,11 @@ template <class T, bool IsProd> struct RAccum {
         else a = IsProd ? a * b : a + b;
     }
     __device__ __forceinline__ static void fold(State& s, T v, int64_t) { combine(s, conv(v)); }
+    // Per-thread state over a chunk of at most 2^31 - 1 positions (see RMinMax::Local).
+    using Local = State;
+    __device__ __forceinline__ static Local local_init() { return init(); }
+    __device__ __forceinline__ static void fold_local(Local& s, T v, int32_t) { combine(s, conv(v)); }
+    __device__ __forceinline__ static State widen(const Local& s, int64_t) { return s; }
     __device__ __forceinline__ static State shfl(State s, int m) { return shfl_xor(s, m); }
     __device__ __forceinline__ static void write(const RedArgs& p, const State& s, int64_t o1, int64_t) {
         if constexpr (is_float_v<T>) static_cast<T*>(p.out)[o1] = static_cast<T>(s);
@@ -112,6 +123,7 @@ template <class T> struct MMState {
 template <class T, bool IsMax, bool Indexed> struct RMinMax {
     using In = T;
     using State = MMState<T>;
+    static constexpr int kUnroll = 4;
     __device__ __forceinline__ static T ident() {
         if constexpr (is_float_v<T>)
             return IsMax ? -std::numeric_limits<T>::infinity() : std::numeric_limits<T>::infinity();
@@ -134,14 +146,37 @@ template <class T, bool IsMax, bool Indexed> struct RMinMax {
     // state that has only met the identity value (+-inf, or the integer limit) keeps the "empty"
     // position INT64_MAX; `combine` applies the full rule, and `write` maps an all-identity
     // slice to position 0, its first element.
+    // take v when the state is not NaN and v is NaN or strictly better: for floats that is
+    // "s.v is a number and not (v <= s.v)" (not (v >= s.v) for min), two compares.
+    __device__ __forceinline__ static bool takes(T sv, T v) {
+        if constexpr (is_float_v<T>) return (sv == sv) && !(IsMax ? v <= sv : v >= sv);
+        else return IsMax ? v > sv : v < sv;
+    }
     __device__ __forceinline__ static void fold(State& s, T v, int64_t j) {
-        bool take;
-        if constexpr (is_float_v<T>) take = (s.v == s.v) && ((v != v) || (IsMax ? v > s.v : v < s.v));
-        else take = IsMax ? v > s.v : v < s.v;
-        if (take) {
+        if (takes(s.v, v)) {
             s.v = v;
             s.i = j;
         }
+    }
+    // A thread's state over one chunk of positions [base, base + 2^31 - 1): the position is kept
+    // as a 32-bit offset from base (one register and one select less per element); widen()
+    // turns it back into the 64-bit state, keeping "empty" as INT64_MAX.
+    struct Local {
+        T v;
+        int32_t i;
+    };
+    __device__ __forceinline__ static Local local_init() {
+        return Local{ident(), std::numeric_limits<int32_t>::max()};
+    }
+    __device__ __forceinline__ static void fold_local(Local& s, T v, int32_t j) {
+        if (takes(s.v, v)) {
+            s.v = v;
+            s.i = j;
+        }
+    }
+    __device__ __forceinline__ static State widen(const Local& s, int64_t base) {
+        return State{s.v, s.i == std::numeric_limits<int32_t>::max() ? std::numeric_limits<int64_t>::max()
+                                                                      : base + s.i};
     }
     __device__ __forceinline__ static void combine(State& a, const State& b) {
         if (better(a, b.v, b.i)) a = b;
@@ -207,13 +242,13 @@ __device__ __forceinline__ int64_t red_decode_red(const RedArgs& p, uint64_t j) 
 }
 
 // Folds row[j] for j in [j0, j1) into s, elements spread over nthr threads: scalar head up to
-// the first 16-byte boundary, 16-byte packs kRedUnroll deep, scalar tail.
+// the first 16-byte boundary, 16-byte packs R::kUnroll deep, scalar tail.
 template <class R> __device__ __forceinline__ void fold_contig(const typename R::In* row, int64_t j0,
                                                                int64_t j1, typename R::State& s,
                                                                int tid, int nthr) {
     using T = typename R::In;
     constexpr int V = 16 / sizeof(T);
-    constexpr int U = kRedUnroll;
+    constexpr int U = red_unroll<R>();
     if (j1 <= j0) return;
     const uintptr_t addr = reinterpret_cast<uintptr_t>(row + j0);
     const int64_t head = static_cast<int64_t>(((16u - (addr & 15u)) & 15u) / sizeof(T));
@@ -284,11 +319,13 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_warp(R
 
 // Column strips: kept inner dim N contiguous, reduced dim K with stride strideK, batch dims in
 // front. CTA = 8 warps; warp w folds rows k0+w, k0+w+8, ... of a 32*V-column strip.
-template <class R, int V> __global__ void __launch_bounds__(kRedBlock) red_outer(RedArgs p) {
+template <class R, int V> __global__ void __launch_bounds__(kOuterBlock) red_outer(RedArgs p) {
     using T = typename R::In;
     using S = typename R::State;
-    constexpr int W = kRedBlock / 32;
-    constexpr int U = kRedUnroll;
+    constexpr int W = kOuterBlock / 32;
+    // rows in flight per warp: a column strip is one 16-byte pack per lane per row, so keep 8 rows
+    // of 4-byte elements (4 KiB per warp) outstanding
+    constexpr int U = sizeof(T) <= 4 ? 8 : 4;
     __shared__ S smem[W - 1][32 * V];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t tiles_n = static_cast<int64_t>(p.aux.d);
@@ -312,9 +349,10 @@ template <class R, int V> __global__ void __launch_bounds__(kRedBlock) red_outer
         const int64_t col0 = static_cast<int64_t>(tn) * (32 * V) + lane * V;
         const int64_t k0 = static_cast<int64_t>(sp) * p.chunk;
         const int64_t k1 = k0 + p.chunk < p.K ? k0 + p.chunk : p.K;
-        S st[V];
+        // positions are folded as 32-bit offsets from k0 (the plan keeps chunks below 2^31)
+        typename R::Local lst[V];
 #pragma unroll
-        for (int e = 0; e < V; ++e) st[e] = R::init();
+        for (int e = 0; e < V; ++e) lst[e] = R::local_init();
         const T* base = static_cast<const T*>(p.in) + in_off + col0;
         if (col0 + V <= p.N) {
             for (int64_t k = k0 + warp; k < k1; k += W * U) {
@@ -328,18 +366,23 @@ template <class R, int V> __global__ void __launch_bounds__(kRedBlock) red_outer
                 for (int u = 0; u < U; ++u) {
                     const int64_t kk = k + u * W;
                     if (kk < k1) {
+                        const int32_t j = static_cast<int32_t>(kk - k0);
 #pragma unroll
-                        for (int e = 0; e < V; ++e) R::fold(st[e], x[u].v[e], kk);
+                        for (int e = 0; e < V; ++e) R::fold_local(lst[e], x[u].v[e], j);
                     }
                 }
             }
         } else {
             for (int64_t k = k0 + warp; k < k1; k += W) {
+                const int32_t j = static_cast<int32_t>(k - k0);
 #pragma unroll
                 for (int e = 0; e < V; ++e)
-                    if (col0 + e < p.N) R::fold(st[e], base[k * p.strideK + e], k);
+                    if (col0 + e < p.N) R::fold_local(lst[e], base[k * p.strideK + e], j);
             }
         }
+        S st[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) st[e] = R::widen(lst[e], k0);
         if (warp > 0) {
 #pragma unroll
             for (int e = 0; e < V; ++e) smem[warp - 1][lane * V + e] = st[e];
@@ -446,8 +489,8 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
     case RedPath::Outer: {
         using T = typename R::In;
         constexpr int VMAX = outer_vec<T>();
-        if (plan.col_tile == 32 * VMAX) red_outer<R, VMAX><<<plan.grid, kRedBlock, 0, st>>>(a);
-        else red_outer<R, 1><<<plan.grid, kRedBlock, 0, st>>>(a);
+        if (plan.col_tile == 32 * VMAX) red_outer<R, VMAX><<<plan.grid, kOuterBlock, 0, st>>>(a);
+        else red_outer<R, 1><<<plan.grid, kOuterBlock, 0, st>>>(a);
         break;
     }
     case RedPath::General:
@@ -489,8 +532,8 @@ int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint
     RedOcc occ;
     occ.inner_cta = resident_ctas(reinterpret_cast<const void*>(&red_inner_cta<R>), kRedBlock);
     occ.inner_warp = resident_ctas(reinterpret_cast<const void*>(&red_inner_warp<R>), kRedBlock);
-    occ.outer = vec_ok ? resident_ctas(reinterpret_cast<const void*>(&red_outer<R, V>), kRedBlock)
-                       : resident_ctas(reinterpret_cast<const void*>(&red_outer<R, 1>), kRedBlock);
+    occ.outer = vec_ok ? resident_ctas(reinterpret_cast<const void*>(&red_outer<R, V>), kOuterBlock)
+                       : resident_ctas(reinterpret_cast<const void*>(&red_outer<R, 1>), kOuterBlock);
     occ.general_cta = resident_ctas(reinterpret_cast<const void*>(&red_general_cta<R>), kRedBlock);
     need = finish_reduction_plan(plan, sizeof(T), sizeof(typename R::State), vec_ok ? V : 1, occ);
     return CTB_OK;

@@ -186,6 +186,19 @@ def binary_chain(op1: str, op2: str, a, b, c) -> torch.Tensor:
     return out
 
 
+def binary_unary(op: str, uop: str, a, b) -> torch.Tensor:
+    """uop(op(a, b)) in one pass (uop: relu, neg or abs), bit-identical to the two eager ops; a and b
+    share one dtype."""
+    codes = {"add": C.ADD, "sub": C.SUB, "mul": C.MUL, "div": C.DIV}
+    ucodes = {"relu": C.RELU, "neg": C.NEG, "abs": C.ABS}
+    dev = _cuda("binary_unary", a, b)
+    out = torch.empty(broadcast_shape(a.shape, b.shape), dtype=a.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _call(C.lib.ctb_binary_unary(codes[op], ucodes[uop], C.view(a), C.view(b), C.view(out),
+                                     C.stream_handle(dev)), "binary_unary")
+    return out
+
+
 def chain_rows(op1: str, op2: str, a, b, c, row_op: str = "min", write_y: bool = True,
                want_sum: bool = True, out_sum: torch.Tensor | None = None):
     """One pass over a [rows, cols] matrix: y = op2(op1(a, b), c) with b, c one broadcast row,

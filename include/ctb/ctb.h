@@ -107,6 +107,14 @@ CTB_API int ctb_binary(int op, const ctb_view* a, const ctb_view* b, const ctb_v
 CTB_API int ctb_binary_chain(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
                      int32_t mid_dtype, const ctb_view* out, ctb_stream stream);
 
+/* out = unary_op(op(a, b)) in one pass (unary_op CTB_RELU, CTB_NEG or CTB_ABS), for a, b and out of
+ * one dtype (int32/int64/float32/float64), broadcasting as ctb_binary. The binary result is rounded
+ * to the dtype before the unary op sees it, so the result is bit-identical to ctorch's
+ * relu(add(a, b)) and the like (two front-door calls, src/ops/binary_ops_cpu.cpp:251-254 and
+ * src/ops/unary_ops_cpu.cpp:160-167) without writing and re-reading the intermediate. */
+CTB_API int ctb_binary_unary(int op, int unary_op, const ctb_view* a, const ctb_view* b,
+                             const ctb_view* out, ctb_stream stream);
+
 /* out = op(in), same shape and dtype. Replaces the UnaryFn CUDA slots (op_keys.h:67-92; reference
  * src/ops/unary_ops_cuda.cu:50-101). neg/abs/relu accept int32/int64/float32/float64;
  * exp/log/sqrt/sigmoid/tanh accept float32/float64 only; bool and bfloat16 give CTB_ERR_DTYPE. */

@@ -98,10 +98,14 @@ def test_planner_hot_path_shapes():
     o4 = view(C, [64, 512, 1024])
     ft = view(C, [64, 512, 1024], [524288, 1, 512])
     assert plan_ew(C, o4, [view(C, [64, 512, 1024], dtype=2), ft])[0] == "tiled"
-    # config 4 div: P[64,512,1024] / D[1,512,1] -> rows of 256 packs with a per-row scalar
+    # config 4 div: P[64,512,1024] / D[1,512,1] -> rows of 256 packs with a per-row scalar, in
+    # warp tiles of 128 packs
     o4d = view(C, [64, 512, 1024], dtype=1)
     assert plan_ew(C, o4d, [view(C, [64, 512, 1024]), view(C, [1, 512, 1], dtype=1)]) == \
-        ("rows_short", [64, 512, 1024])
+        ("rows_mid", [64, 512, 1024])
+    # rows of 127 packs are short, 128 mid, 1023 mid, 1024 long
+    for cols, path in ((508, "rows_short"), (512, "rows_mid"), (4092, "rows_mid"), (4096, "rows_long")):
+        assert plan_ew(C, view(C, [64, cols]), [view(C, [64, cols]), view(C, [64, 1])])[0] == path
     # config 5 fused chain: (X - r) * r with r [1, 8192]
     o5 = view(C, [32768, 8192])
     assert plan_ew(C, o5, [view(C, [32768, 8192]), view(C, [1, 8192]), view(C, [1, 8192])])[0] == "rows_long"

@@ -40,6 +40,9 @@ BIN_LAYOUTS = {
     "flat_scalar": ((777_777,), [], (), []),
     "rows_long": ((384, 4096), [], (1, 4096), []),
     "rows_long_col": ((300, 8192), [], (300, 1), []),
+    "rows_mid": ((300, 1000), [], (1, 1000), []),
+    "rows_mid_col": ((200, 4092), [], (200, 1), []),
+    "rows_long_wide": ((40, 8200), [], (1, 8200), []),
     "rows_short": ((20_000, 12), [], (1, 12), []),
     "rows_short_3d": ((50, 40, 8), [], (40, 1), []),
     "tiled": ((6, 200, 300), [], (6, 300, 200), [("permute", [0, 2, 1])]),
@@ -380,3 +383,89 @@ def test_sharded_step_fused_matches_three_kernel_step(cuda_ok):
     assert torch.equal(y1, y2)
     assert torch.equal(k1, k2)
     assert abs(float(s1) - float(s2)) <= 1e-6 * max(1.0, abs(float(s1)))
+
+
+@pytest.mark.parametrize("uop", ["relu", "neg", "abs"])
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div"])
+@pytest.mark.parametrize("dt", [np.float32, np.float64, np.int32, np.int64])
+def test_binary_unary_is_bitwise_the_eager_pair(cuda_ok, oracle, op, uop, dt):
+    import ctorch_b200 as cb
+
+    if op == "div" and np.dtype(dt).kind == "i":
+        pytest.skip("integer division is refused")
+    rng = np.random.default_rng(_seed(op, uop, np.dtype(dt).name))
+    for layout in ("rows_long", "flat_tail", "rows_short", "general_offset"):
+        sa, ra, sb, rb = BIN_LAYOUTS[layout]
+        a, ta = _pair(_rand(rng, sa, dt), ra)
+        b, tb = _pair(_rand(rng, sb, dt), rb)
+        got = cb.binary_unary(op, uop, ta, tb).cpu().numpy()
+        ref = oracle.unary(uop, oracle.binary(op, a, b))
+        assert_bitexact(got, ref, f"{uop}({op}) {layout}", nan_payload=False)
+
+
+def _special_divisors(dt):
+    """Per-row divisors that probe the reciprocal path of a division by a per-row scalar: unit and
+    power-of-two scales, all-ones significands, the exponents on either side of the range where
+    the reciprocal is used, and zeros, infinities, NaN and subnormals (which take the IEEE
+    division)."""
+    dt = np.dtype(dt)
+    if dt == np.float32:
+        ui, mant, margin, emax = np.uint32, 23, 32, 254
+    else:
+        ui, mant, margin, emax = np.uint64, 52, 64, 2046
+    ones = (1 << mant) - 1
+    pats = []
+    for e in (1, margin - 1, margin, margin + 1, emax // 2 - 1, emax // 2, emax // 2 + 1,
+              emax - margin - 1, emax - margin, emax - margin + 1, emax):
+        for m in (0, ones, 1, ones >> 1, 0x5 << (mant - 3)):
+            pats.append((e << mant) | m)
+    pats += [0, 1, ones, (emax + 1) << mant, ((emax + 1) << mant) | 1]  # 0, subnormals, inf, NaN
+    v = np.array(pats, dtype=ui).view(dt)
+    return np.concatenate([v, -v, np.array([3, 7, 0.1, 1 / 3, 10, -5e-3], dtype=dt)])
+
+
+def _dividends(rng, n, dt):
+    """Half uniform over every bit pattern (all exponents, NaN, inf, subnormals), half ordinary
+    values."""
+    dt = np.dtype(dt)
+    ui = np.uint32 if dt.itemsize == 4 else np.uint64
+    raw = rng.integers(0, np.iinfo(ui).max, n, dtype=ui, endpoint=True).view(dt)
+    ordinary = (rng.standard_normal(n) * np.exp2(rng.integers(-20, 20, n))).astype(dt)
+    return np.where(rng.random(n) < 0.5, raw, ordinary)
+
+
+ROW_DIV = [
+    # (x shape, divisor shape, x dtype, divisor dtype): the kernel each one plans to
+    ((300, 1024), (300, 1), np.float32, np.float32),    # rows_mid
+    ((300, 1024), (300, 1), np.float32, np.float64),    # rows_mid, promoted to float64
+    ((128, 1000), (128, 1), np.float64, np.float64),    # rows_mid, last tile of each row partial
+    ((300, 8192), (300, 1), np.float32, np.float32),    # rows_long, 2048 packs a row
+    ((100, 5000), (100, 1), np.float32, np.float32),    # rows_long, 1250 packs a row
+    ((96, 8200), (96, 1), np.float64, np.float64),      # rows_long with a tail
+    ((3000, 100), (3000, 1), np.float64, np.float64),   # rows_short, 50 packs a row
+    ((2000, 12), (2000, 1), np.float32, np.float32),    # rows_short, 3 packs a row
+    ((4, 512, 1024), (1, 512, 1), np.float32, np.float64),  # the float32 / float64[1,512,1] shape
+]
+
+
+@pytest.mark.parametrize("sx,sd,dx,dd", ROW_DIV, ids=[f"{'x'.join(map(str, c[0]))}-{np.dtype(c[2]).name}-{np.dtype(c[3]).name}" for c in ROW_DIV])
+def test_division_by_a_per_row_scalar_is_correctly_rounded(cuda_ok, oracle, sx, sd, dx, dd):
+    import torch
+
+    import ctorch_b200 as cb
+
+    rng = np.random.default_rng(_seed("rowdiv", sx, sd))
+    x = _dividends(rng, int(np.prod(sx)), dx).reshape(sx)
+    rows = int(np.prod(sd))
+    special = _special_divisors(dd)
+    d = _dividends(rng, rows, dd)
+    d[: min(rows, special.size)] = special[:rows]
+    rng.shuffle(d)
+    d = d.reshape(sd)
+    # exact quotients: a few rows hold small multiples of their divisor
+    flat_x = x.reshape(-1, sx[-1])
+    flat_d = np.broadcast_to(d, sx[:-1] + (1,)).reshape(-1, 1)
+    k = rng.integers(-64, 64, (4, sx[-1])).astype(dx)
+    flat_x[:4] = (flat_d[:4].astype(np.float64) * k).astype(dx)
+    got = cb.div(torch.from_numpy(x).cuda(), torch.from_numpy(d).cuda()).cpu().numpy()
+    assert_bitexact(got, oracle.binary("div", x, d), f"div {sx} / {sd}", nan_payload=False)
