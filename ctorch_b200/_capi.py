@@ -84,6 +84,8 @@ def _load() -> ctypes.CDLL:
                                            ctypes.POINTER(ctypes.c_int),
                                            ctypes.POINTER(ctypes.c_int)]),
         "ctb_debug_fastdiv": (u64, [u64, u64]),
+        "ctb_wait_timeouts": (i32, [ctypes.POINTER(ctypes.c_uint64)]),
+        "ctb_debug_wait_timeout": (i32, [u64, ctypes.POINTER(ctypes.c_int)]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -120,3 +122,12 @@ def view(t: torch.Tensor | None) -> View | None:
 
 def stream_handle(device: torch.device | None = None) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def wait_timeouts() -> int:
+    """Timed-out waits counted on the current device (ctb_wait_timeouts); 0 on a healthy GPU."""
+    n = ctypes.c_uint64(0)
+    rc = lib.ctb_wait_timeouts(ctypes.byref(n))
+    if rc != OK:
+        raise RuntimeError(last_error())
+    return n.value

@@ -391,8 +391,11 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
     RedArgs& a = plan.args;
     const int64_t sms = sm_count();
     plan.block = 256;
+    plan.bulk = false;
+    plan.bulk_fixup = false;
     a.split = 1;
     a.chunk = a.red;
+    a.sk_q = a.sk_r = 0;
     size_t scratch = 0;
     switch (plan.path) {
     case RedPath::Empty:
@@ -430,6 +433,34 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
         break;
     }
     case RedPath::Outer: {
+        if (occ.cols_bulk > 0) {
+            // Stream-K over (column tile, row): G CTAs take equal shares of the row-steps, so
+            // every CTA streams the same number of bytes whatever the tile count; a tile shared
+            // by several CTAs is combined in CTA order by red_cols_finalize.
+            plan.bulk = true;
+            plan.block = kColsThreads;
+            const int64_t tw = kColsRowBytes / elem_bytes;  // columns per tile
+            const int64_t tiles_n = (a.N + tw - 1) / tw;
+            const int64_t tiles = tiles_n * (a.kept / a.N);
+            const int64_t steps = tiles * a.K;
+            const int64_t slots = sms * occ.cols_bulk;
+            // partial states (one row of tw per CTA-and-tile pair, G + tiles - 1 pairs at most)
+            // are held to 4 MiB
+            const int64_t cap = std::max<int64_t>(1, (int64_t(4) << 20) / (tw * state_bytes) - tiles);
+            int64_t G = std::min<int64_t>({slots, cap, std::max<int64_t>(1, steps / (2 * kColsRows))});
+            G = std::max<int64_t>(1, std::min<int64_t>(G, steps));
+            a.sk_q = steps / G;
+            a.sk_r = steps % G;
+            a.aux = FastDiv(static_cast<uint64_t>(tiles_n));
+            a.aux2 = FastDiv(static_cast<uint64_t>(a.K));
+            plan.grid = static_cast<unsigned>(G);
+            plan.bulk_tiles = tiles;
+            plan.bulk_fixup = false;
+            for (int64_t c = 1; c < G && !plan.bulk_fixup; ++c)
+                if ((c * a.sk_q + std::min<int64_t>(c, a.sk_r)) % a.K != 0) plan.bulk_fixup = true;
+            if (plan.bulk_fixup) scratch = static_cast<size_t>(G + tiles) * tw * state_bytes;
+            break;
+        }
         plan.col_tile = 32 * outer_vec;
         const int64_t tiles_n = (a.N + plan.col_tile - 1) / plan.col_tile;
         const int64_t batch = a.kept / a.N;

@@ -108,7 +108,12 @@ struct RedArgs {
     FastDiv div_k[kMaxDims];
     FastDiv div_r[kMaxDims];
     FastDiv aux;        // Outer: column tiles; Inner: splits
-    FastDiv aux2;       // Outer: splits
+    FastDiv aux2;       // Outer: splits (bulk column kernel: the reduced extent K)
+    // Bulk column kernel: CTA c folds the row-steps [c*sk_q + min(c, sk_r), ...) of the
+    // flattened (column tile, row) space, sk_q or sk_q + 1 of them. CTA c's partial for tile s
+    // (when it shares s with other CTAs) is partial row c + s of the scratch.
+    int64_t sk_q, sk_r;
+    unsigned long long* timeouts;  // device counter of timed-out waits (async_copy.cuh)
 };
 
 struct RedPlan {
@@ -119,6 +124,9 @@ struct RedPlan {
     unsigned grid = 1;
     bool warp_rows = false;  // Inner: one warp per row instead of one CTA per row
     int col_tile = 0;        // Outer: columns per CTA
+    bool bulk = false;       // Outer: bulk-copy column kernel (red_cols_bulk) instead of red_outer
+    bool bulk_fixup = false; // bulk: some column tile is shared by several CTAs (second pass)
+    int64_t bulk_tiles = 0;  // bulk: column tiles
 };
 
 // Builds the kept/reduced split of `in` for the given mask and output view(s) (out2 may be null),
@@ -132,7 +140,15 @@ int plan_reduction(const ctb_view* in, const ctb_view* out, const ctb_view* out2
 // reducer); grids are sized to whole waves of these.
 struct RedOcc {
     int inner_cta = 4, inner_warp = 4, outer = 4, general_cta = 4;
+    int cols_bulk = 0;  // resident bulk column CTAs per SM; 0 when that kernel cannot take the plan
 };
+
+// Bulk column kernel geometry: each CTA has 4 consumer warps and 1 producer warp. A column tile
+// is 2 KiB of a row (128 threads x one 16-byte pack of columns each), a stage holds 8 rows of it.
+constexpr int kColsConsumers = 128;
+constexpr int kColsRowBytes = 2048;
+constexpr int kColsRows = 8;
+constexpr int kColsThreads = kColsConsumers + 32;
 
 // Chooses split counts / grid for a planned reduction. `state_bytes` is the size of one partial
 // state, `outer_vec` the column-strip pack width the Outer kernel will use; returns the scratch

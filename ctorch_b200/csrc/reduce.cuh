@@ -21,7 +21,9 @@
 #pragma once
 
 #include <limits>
+#include <mutex>
 
+#include "async_copy.cuh"
 #include "common.cuh"
 #include "plan.cuh"
 
@@ -407,6 +409,226 @@ template <class R, int V> __global__ void __launch_bounds__(kOuterBlock) red_out
     }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Column reductions through a shared-memory stage ring filled by bulk asynchronous copies
+// (async_copy.cuh). Warp 4 is the producer: for each stage it copies 8 rows of a column tile (2 KiB
+// of each row, one bulk copy per row, issued by one lane each) into shared memory. Warps 0-3 are
+// consumers: thread t owns one 16-byte pack of the tile's columns (4 float columns) and folds them
+// down the stage in row order, one independent chain per column, so the fold order per output is
+// the row order, as in ctorch's sequential fold. The CTA's loads are in flight in the copy engine,
+// not in registers: 6 stages of 16 KiB keep 96 KiB per CTA moving.
+//
+// Work split (stream-K): the column tiles x rows form one sequence of row-steps; CTA c takes an
+// equal contiguous share of it (RedArgs::sk_q, sk_r). A tile a CTA covers whole is written
+// directly; a tile s shared by several CTAs gets one partial state per column from each CTA c
+// that touches it (scratch row c + s), combined in CTA order by red_cols_finalize.
+
+constexpr int kColsStages = 6;
+template <class T> constexpr int cols_tile() { return kColsRowBytes / static_cast<int>(sizeof(T)); }
+constexpr size_t cols_smem_bytes() {
+    return static_cast<size_t>(kColsStages) * kColsRows * kColsRowBytes + 2 * kColsStages * sizeof(uint64_t);
+}
+
+// Tile s of the bulk column kernel: input offset of its first column, output offsets of its
+// batch row, and its first column.
+template <class T>
+__device__ __forceinline__ void cols_tile_at(const RedArgs& p, uint64_t s, int64_t& in_off, int64_t& o1,
+                                             int64_t& o2, int64_t& col0) {
+    uint64_t b, tn;
+    p.aux.divmod(s, b, tn);
+    in_off = o1 = o2 = 0;
+    for (int d = p.rank_k - 2; d >= 0; --d) {
+        uint64_t q, c;
+        p.div_k[d].divmod(b, q, c);
+        in_off += static_cast<int64_t>(c) * p.stride_k[d];
+        o1 += static_cast<int64_t>(c) * p.stride_o[d];
+        o2 += static_cast<int64_t>(c) * p.stride_o2[d];
+        b = q;
+    }
+    col0 = static_cast<int64_t>(tn) * cols_tile<T>();
+}
+
+__device__ __forceinline__ int64_t cols_start(const RedArgs& p, int64_t c) {
+    return c * p.sk_q + (c < p.sk_r ? c : p.sk_r);
+}
+
+template <class R> __global__ void __launch_bounds__(kColsThreads, 1) red_cols_bulk(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    constexpr int NS = kColsStages;
+    constexpr int VE = 16 / static_cast<int>(sizeof(T));  // columns per consumer thread
+    constexpr int TW = cols_tile<T>();                      // columns per tile
+    constexpr int kStage = kColsRows * TW;                  // elements per stage
+    constexpr int kConsumerWarps = kColsConsumers / 32;
+    extern __shared__ __align__(128) unsigned char cols_smem[];
+    T* stages = reinterpret_cast<T*>(cols_smem);
+    uint64_t* full = reinterpret_cast<uint64_t*>(cols_smem + static_cast<size_t>(NS) * kStage * sizeof(T));
+    uint64_t* empty = full + NS;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kConsumerWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    const int64_t c = blockIdx.x;
+    const int64_t start = cols_start(p, c);
+    const int64_t end = cols_start(p, c + 1);
+    if (warp == kConsumerWarps) {
+        // ---- producer
+        uint32_t g = 0;
+        bool ok = true;
+        for (int64_t pos = start; pos < end && ok;) {
+            uint64_t s, ka;
+            p.aux2.divmod(static_cast<uint64_t>(pos), s, ka);
+            const int64_t kb = min(p.K, static_cast<int64_t>(ka) + (end - pos));
+            int64_t in_off, o1, o2, col0;
+            cols_tile_at<T>(p, s, in_off, o1, o2, col0);
+            const T* src = static_cast<const T*>(p.in) + in_off + col0;
+            const int64_t ncols = min(static_cast<int64_t>(TW), p.N - col0);
+            const uint32_t vb = static_cast<uint32_t>(ncols * static_cast<int64_t>(sizeof(T)));
+            for (int64_t k = static_cast<int64_t>(ka); k < kb; k += kColsRows, ++g) {
+                const int slot = static_cast<int>(g % NS);
+                const bool w = mbar_wait(&empty[slot], ((g / NS) & 1u) ^ 1u);
+                if (!__all_sync(0xffffffffu, w)) {
+                    ok = false;
+                    break;
+                }
+                const int rows = static_cast<int>(min(static_cast<int64_t>(kColsRows), kb - k));
+                if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(rows) * vb);
+                __syncwarp();
+                if (lane < rows)
+                    bulk_load(stages + slot * kStage + lane * TW, src + (k + lane) * p.strideK, vb, &full[slot]);
+            }
+            pos += kb - static_cast<int64_t>(ka);
+        }
+        if (!ok && lane == 0) {
+            note_timeout(p.timeouts);
+            // let the copies already issued land before the CTA's shared memory goes away
+            for (uint32_t i = g > static_cast<uint32_t>(NS) ? g - NS : 0u; i < g; ++i)
+                mbar_wait(&full[i % NS], (i / NS) & 1u);
+        }
+        return;
+    }
+
+    // ---- consumers: thread t folds columns [t*VE, t*VE + VE) of the tile
+    const int t = threadIdx.x;
+    uint32_t g = 0;
+    for (int64_t pos = start; pos < end;) {
+        uint64_t s, ka;
+        p.aux2.divmod(static_cast<uint64_t>(pos), s, ka);
+        const int64_t kb = min(p.K, static_cast<int64_t>(ka) + (end - pos));
+        int64_t in_off, o1, o2, col0;
+        cols_tile_at<T>(p, s, in_off, o1, o2, col0);
+        const int64_t col = col0 + static_cast<int64_t>(t) * VE;
+        const bool active = col < p.N;  // N is a whole number of packs, so a pack is all in or out
+        typename R::Local st[VE];
+#pragma unroll
+        for (int e = 0; e < VE; ++e) st[e] = R::local_init();
+        for (int64_t k = static_cast<int64_t>(ka); k < kb; k += kColsRows, ++g) {
+            const int slot = static_cast<int>(g % NS);
+            const bool w = mbar_wait(&full[slot], (g / NS) & 1u);
+            if (!__all_sync(0xffffffffu, w)) {
+                if (lane == 0) note_timeout(p.timeouts);
+                return;
+            }
+            const int rows = static_cast<int>(min(static_cast<int64_t>(kColsRows), kb - k));
+            const T* sb = stages + slot * kStage + t * VE;
+            const int32_t j0 = static_cast<int32_t>(k - static_cast<int64_t>(ka));
+            if (active) {
+                if (rows == kColsRows) {
+                    Pack<T, VE> x[kColsRows];
+#pragma unroll
+                    for (int j = 0; j < kColsRows; ++j) x[j] = *reinterpret_cast<const Pack<T, VE>*>(sb + j * TW);
+#pragma unroll
+                    for (int j = 0; j < kColsRows; ++j)
+#pragma unroll
+                        for (int e = 0; e < VE; ++e) R::fold_local(st[e], x[j].v[e], j0 + j);
+                } else {
+                    for (int j = 0; j < rows; ++j) {
+                        const Pack<T, VE> x = *reinterpret_cast<const Pack<T, VE>*>(sb + j * TW);
+#pragma unroll
+                        for (int e = 0; e < VE; ++e) R::fold_local(st[e], x.v[e], j0 + j);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        if (active) {
+            const bool whole = ka == 0 && kb == p.K;
+            S* part = static_cast<S*>(p.scratch) + (c + static_cast<int64_t>(s)) * TW + t * VE;
+#pragma unroll
+            for (int e = 0; e < VE; ++e) {
+                const S v = R::widen(st[e], static_cast<int64_t>(ka));
+                if (whole) R::write(p, v, o1 + col + e, o2 + col + e);
+                else part[e] = v;
+            }
+        }
+        pos += kb - static_cast<int64_t>(ka);
+    }
+}
+
+// Second pass of the bulk column kernel: for every column of a tile shared by several CTAs,
+// combine their partial states in CTA order (that is, row order) and write the result. A block
+// takes 32 consecutive outputs (one per lane, so partial loads are coalesced) and splits each one's
+// CTA range into 8 consecutive groups, one per warp; warp 0 then combines the 8 group results in
+// group order. The combine order is fixed by the plan, so results are run-to-run identical.
+constexpr int kColsFixGroups = 8;
+template <class R> __global__ void __launch_bounds__(32 * kColsFixGroups) red_cols_finalize(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    constexpr int TW = cols_tile<T>();
+    __shared__ S red[kColsFixGroups][32];
+    const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+    const S* part = static_cast<const S*>(p.scratch);
+    const int64_t tiles_n = static_cast<int64_t>(p.aux.d);
+    const int64_t big = p.sk_r * (p.sk_q + 1);  // row-steps owned by the CTAs with one extra
+    for (int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32; k0 < p.kept; k0 += static_cast<int64_t>(gridDim.x) * 32) {
+        const int64_t k = k0 + lane;
+        bool shared_tile = false;
+        S st = R::init();
+        if (k < p.kept) {
+            const int64_t b = k / p.N, col = k - b * p.N;
+            const int64_t s = b * tiles_n + col / TW;
+            const int64_t first = s * p.K, last = first + p.K - 1;
+            const int64_t c_lo = first < big ? first / (p.sk_q + 1) : p.sk_r + (first - big) / p.sk_q;
+            const int64_t c_hi = last < big ? last / (p.sk_q + 1) : p.sk_r + (last - big) / p.sk_q;
+            shared_tile = c_lo != c_hi;  // else one CTA covered the whole tile and wrote it
+            if (shared_tile) {
+                const int64_t n = c_hi - c_lo + 1;
+                const int64_t per = (n + kColsFixGroups - 1) / kColsFixGroups;
+                const int64_t ca = c_lo + grp * per;
+                const int64_t cb = min(c_hi + 1, ca + per);
+                const S* col_parts = part + s * TW + col % TW;
+                int64_t cc = ca;
+                for (; cc + 4 <= cb; cc += 4) {
+                    S v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) v[u] = col_parts[(cc + u) * TW];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) R::combine(st, v[u]);
+                }
+                for (; cc < cb; ++cc) R::combine(st, col_parts[cc * TW]);
+            }
+        }
+        red[grp][lane] = st;
+        __syncthreads();
+        if (grp == 0 && shared_tile) {
+            S r = red[0][lane];
+#pragma unroll
+            for (int g2 = 1; g2 < kColsFixGroups; ++g2) R::combine(r, red[g2][lane]);
+            int64_t in_off, o1, o2;
+            red_decode_kept(p, static_cast<uint64_t>(k), in_off, o1, o2);
+            R::write(p, r, o1, o2);
+        }
+        __syncthreads();
+    }
+}
+
 // One thread per output, folding the reduced subspace in row-major order (the CPU's order).
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_thread(RedArgs p) {
     using T = typename R::In;
@@ -488,6 +710,14 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
         break;
     case RedPath::Outer: {
         using T = typename R::In;
+        if (plan.bulk) {
+            red_cols_bulk<R><<<plan.grid, kColsThreads, cols_smem_bytes(), st>>>(a);
+            if (plan.bulk_fixup) {
+                red_cols_finalize<R><<<grid_for((a.kept + 31) / 32, 8), 32 * kColsFixGroups, 0, st>>>(a);
+                ++launches;
+            }
+            break;
+        }
         constexpr int VMAX = outer_vec<T>();
         if (plan.col_tile == 32 * VMAX) red_outer<R, VMAX><<<plan.grid, kOuterBlock, 0, st>>>(a);
         else red_outer<R, 1><<<plan.grid, kOuterBlock, 0, st>>>(a);
@@ -520,6 +750,44 @@ inline bool outer_vec_ok(const RedPlan& plan, int elem_bytes, int V) {
     return true;
 }
 
+// Whether the bulk column kernel can take this Outer plan: every row of every tile starts on a
+// 16-byte boundary and every row copy is a whole number of 16-byte chunks; positions within the
+// reduced dim fit the kernel's 32-bit offsets.
+inline bool cols_bulk_ok(const RedPlan& plan, int elem_bytes) {
+    const RedArgs& a = plan.args;
+    if (plan.path != RedPath::Outer) return false;
+    if (reinterpret_cast<uintptr_t>(a.in) % 16) return false;
+    if ((a.N * elem_bytes) % 16 || (a.strideK * elem_bytes) % 16) return false;
+    for (int d = 0; d < a.rank_k - 1; ++d)
+        if ((a.stride_k[d] * elem_bytes) % 16) return false;
+    // at least a quarter of the consumer threads busy; narrower strips go to red_outer
+    if (a.N * elem_bytes < kColsRowBytes / 4) return false;
+    return a.K < (int64_t(1) << 31) - 1;
+}
+
+// Address of this device's timed-out-wait counter (async.cu); null if it cannot be had.
+unsigned long long* wait_timeout_counter();
+
+// Lets red_cols_bulk<R> use its dynamic shared memory on the current device (once per device).
+template <class R> bool cols_bulk_ready() {
+    static std::mutex mu;
+    static signed char state[64] = {};  // 0 unknown, 1 ready, -1 unavailable
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return false;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (state[dev] == 0) {
+        const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&red_cols_bulk<R>),
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(cols_smem_bytes()));
+        if (e != cudaSuccess) cudaGetLastError();
+        state[dev] = e == cudaSuccess ? 1 : -1;
+    }
+    return state[dev] == 1;
+}
+
 // Plans + sizes a reduction for reducer R; returns scratch bytes via `need`.
 template <class R>
 int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint32_t mask,
@@ -530,6 +798,12 @@ int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint
     constexpr int V = outer_vec<T>();
     const bool vec_ok = outer_vec_ok(plan, sizeof(T), V);
     RedOcc occ;
+    if (cols_bulk_ok(plan, sizeof(T)) && cols_bulk_ready<R>()) {
+        plan.args.timeouts = wait_timeout_counter();
+        if (plan.args.timeouts)
+            occ.cols_bulk = resident_ctas(reinterpret_cast<const void*>(&red_cols_bulk<R>), kColsThreads,
+                                          cols_smem_bytes());
+    }
     occ.inner_cta = resident_ctas(reinterpret_cast<const void*>(&red_inner_cta<R>), kRedBlock);
     occ.inner_warp = resident_ctas(reinterpret_cast<const void*>(&red_inner_warp<R>), kRedBlock);
     occ.outer = vec_ok ? resident_ctas(reinterpret_cast<const void*>(&red_outer<R, V>), kOuterBlock)

@@ -87,6 +87,14 @@ CTB_API const char* ctb_last_error(void);
 CTB_API uint64_t ctb_launch_count(void);
 CTB_API void ctb_launch_count_reset(void);
 
+/* Number of waits that timed out on the current device since the library was loaded. Kernels that
+ * stream through shared memory with bulk asynchronous copies (the column reductions of
+ * ctb_reduce / ctb_reduce_index) bound every wait to about a second; a wait that runs out is
+ * counted here, and the kernel returns without writing its outputs instead of hanging. A
+ * healthy device reports 0. Synchronous (reads device memory). No ctorch counterpart: ctorch's
+ * kernels have no waits. */
+CTB_API int ctb_wait_timeouts(uint64_t* count);
+
 /* out = op(a, b), elementwise with right-aligned broadcasting of a and b to out's shape.
  * Replaces ctorch's BinaryFn CUDA slots (include/ctorch/ops/op_keys.h:33-46; reference kernels
  * src/ops/binary_ops_cuda.cu:53-112) and, with out == a, the BinaryInplaceFn slots (:50-62).

@@ -1,7 +1,7 @@
 /*
- * ctb_debug.h — host-only introspection of the B200 backend's planner. These functions make no
- * CUDA call that needs a device, so the planner can be tested on a machine without a GPU. They
- * have no counterpart in ctorch (ctorch builds its iteration plans inline:
+ * ctb_debug.h — host-only introspection of the B200 backend's planner, plus a GPU self-test of
+ * the bounded wait. The planner functions make no CUDA call that needs a device, so the planner
+ * can be tested on a machine without a GPU. They have no counterpart in ctorch (ctorch builds its iteration plans inline:
  * src/ops/tensor_iter.cpp:41-84, src/ops/reduction_iter.cpp:20-69).
  */
 #ifndef CTB_CTB_DEBUG_H
@@ -25,6 +25,12 @@ CTB_API int ctb_debug_plan_reduction(const ctb_view* in, const ctb_view* out, ui
 
 /* floor(n / d) through the kernels' invariant-divisor multiply (n < 2^63, d >= 1). */
 CTB_API uint64_t ctb_debug_fastdiv(uint64_t n, uint64_t d);
+
+/* Self-test of the bounded wait (needs a GPU, unlike the functions above): one thread waits on a
+ * shared-memory barrier that nothing arrives at, for limit_ns (at most 100 ms), then returns.
+ * *completed is 0 when the wait timed out, as it must; the timeout is also counted by
+ * ctb_wait_timeouts. Synchronous. */
+CTB_API int ctb_debug_wait_timeout(uint64_t limit_ns, int* completed);
 
 #ifdef __cplusplus
 }

@@ -469,3 +469,80 @@ def test_division_by_a_per_row_scalar_is_correctly_rounded(cuda_ok, oracle, sx, 
     flat_x[:4] = (flat_d[:4].astype(np.float64) * k).astype(dx)
     got = cb.div(torch.from_numpy(x).cuda(), torch.from_numpy(d).cuda()).cpu().numpy()
     assert_bitexact(got, oracle.binary("div", x, d), f"div {sx} / {sd}", nan_payload=False)
+
+
+BULK_COLS = [
+    # (shape, reduced dim): column reductions the bulk-copy kernel takes (rows of at least 512
+    # bytes, a whole number of 16-byte chunks), from one stage to thousands, with tiles shared by
+    # CTAs; the narrower dtypes of some shapes go to the register kernel instead
+    ((8192, 2048), 0),
+    ((100_000, 128), 0),
+    ((33, 512), 0),
+    ((5, 128), 0),
+    ((1, 20_000), 0),
+    ((4, 300, 272), 1),
+    ((7, 65, 304), 1),
+    ((3000, 528), 0),
+    ((2000, 1024), 0),
+]
+
+
+@pytest.mark.parametrize("shape,dim", BULK_COLS, ids=["x".join(map(str, s)) + f"-d{d}" for s, d in BULK_COLS])
+def test_column_reductions_through_the_bulk_copy_ring(cuda_ok, oracle, shape, dim):
+    from ctorch_b200 import _capi as C
+
+    import ctorch_b200 as cb
+
+    before = C.wait_timeouts()
+    rng = np.random.default_rng(_seed("bulk", shape, dim))
+    for dt in (np.float32, np.float64, np.int32, np.int64, np.bool_):
+        base = _rand(rng, shape, dt)
+        if np.dtype(dt).kind == "i":
+            base = (base % 5).astype(dt)  # ties: the first row must win
+        if np.dtype(dt).kind == "f":
+            base = (np.round(base * 4) / 4).astype(dt)
+            base.flat[::997] = np.nan
+            base.flat[3::389] = -0.0
+        x, tx = _pair(base, [])
+        name = np.dtype(dt).name
+        for op in ("max", "min"):
+            v, i = getattr(cb, op)(tx, dim, False)
+            rv, ri = oracle.reduce_idx(op, x, dim, False)
+            assert_bitexact(v.cpu().numpy(), rv, f"{op} values {shape} {name}")
+            assert_bitexact(i.cpu().numpy(), ri, f"{op} indices {shape} {name}")
+            got = getattr(cb, op)(tx, [dim], True).cpu().numpy()
+            assert_bitexact(got, oracle.reduce(op, x, [dim], True), f"{op} {shape} {name}")
+        if np.dtype(dt).kind == "f":
+            fx = np.nan_to_num(x, nan=0.5)
+            _, tfx = _pair(fx, [])
+            got = cb.sum(tfx, [dim], False).cpu().numpy()
+            assert_close(got, oracle.reduce("sum", fx, [dim], False), TOL_SUM[np.dtype(dt)], f"sum {shape} {name}")
+            px = (1 + 1e-4 * fx).astype(dt)
+            _, tpx = _pair(px, [])
+            got = cb.prod(tpx, [dim], False).cpu().numpy()
+            assert_close(got, oracle.reduce("prod", px, [dim], False), TOL_SUM[np.dtype(dt)], f"prod {shape} {name}")
+        else:
+            got = cb.sum(tx, [dim], False).cpu().numpy()
+            assert_bitexact(got, oracle.reduce("sum", x, [dim], False), f"sum {shape} {name}")
+    assert C.wait_timeouts() == before, "a bulk-copy wait timed out"
+
+
+def test_bounded_wait_times_out_and_the_device_stays_usable(cuda_ok):
+    """A wait on a barrier that nothing arrives at must give up after its limit, be counted, and
+    leave the context working (no trap, no hang)."""
+    import ctypes
+
+    import torch
+
+    from ctorch_b200 import _capi as C
+
+    import ctorch_b200 as cb
+
+    before = C.wait_timeouts()
+    done = ctypes.c_int(-1)
+    rc = C.lib.ctb_debug_wait_timeout(5_000_000, ctypes.byref(done))  # 5 ms
+    assert rc == C.OK, C.last_error()
+    assert done.value == 0
+    assert C.wait_timeouts() == before + 1
+    x = torch.arange(12, dtype=torch.float32, device="cuda").reshape(3, 4)
+    assert cb.sum(x).item() == 66.0
