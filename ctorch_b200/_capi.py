@@ -76,6 +76,7 @@ def _load() -> ctypes.CDLL:
         "ctb_sum_partial_scratch_bytes": (sz, [P]),
         "ctb_sum_partial": (i32, [P, vp, vp, sz, vp]),
         "ctb_sum_combine": (i32, [vp, i32, P, vp]),
+        "ctb_minmax_combine": (i32, [i32, P, P, vp, P, P, vp]),
         "ctb_fill_random": (i32, [P, i32, u64, u64, i64, ctypes.c_double, ctypes.c_double, vp]),
         "ctb_debug_plan_elementwise": (i32, [P, ctypes.POINTER(P), i32, i32, ctypes.c_char_p, i32,
                                              ctypes.POINTER(ctypes.c_int),

@@ -31,6 +31,8 @@ int minmax_dispatch(int op, const ctb_view* in, const ctb_view* values, const ct
 int sum_partial_dispatch(const ctb_view* in, double* d_partial, void* scratch, size_t sb,
                          cudaStream_t st, size_t* need_only);
 int sum_combine(const double* parts, int n, const ctb_view* out, cudaStream_t st);
+int minmax_combine(int op, const ctb_view* values, const ctb_view* indices, const int64_t* d_offsets,
+                   const ctb_view* out_values, const ctb_view* out_indices, cudaStream_t st);
 int index_select_dispatch(const ctb_view* src, int dim, const ctb_view* idx, const ctb_view* out,
                           int32_t* status, cudaStream_t st);
 int fill_random(const ctb_view* out, int dist, uint64_t seed, uint64_t stream_id, int64_t first,
@@ -434,6 +436,31 @@ int ctb_sum_combine(const double* d_partials, int n, const ctb_view* out, ctb_st
             return fail(CTB_ERR_DTYPE, "combined sum must be float32/float64");
         if (view_numel(out) != 1) return fail(CTB_ERR_SHAPE, "combined sum output must hold one element");
         return sum_combine(d_partials, n, out, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int ctb_minmax_combine(int op, const ctb_view* values, const ctb_view* indices, const int64_t* d_row_offsets,
+                       const ctb_view* out_values, const ctb_view* out_indices, ctb_stream stream) {
+    return guarded([&]() -> int {
+        t_error.clear();
+        if (op != CTB_MAX && op != CTB_MIN) return fail(CTB_ERR_ARGUMENT, "op must be CTB_MAX or CTB_MIN");
+        if (int rc = check_views({values, indices, out_indices})) return rc;
+        if (out_values)
+            if (int rc = check_views({out_values})) return rc;
+        if (!d_row_offsets) return fail(CTB_ERR_ARGUMENT, "null row offsets");
+        if (values->ndim != 2 || indices->ndim != 2 || out_indices->ndim != 1 || (out_values && out_values->ndim != 1))
+            return fail(CTB_ERR_SHAPE, "shard results must be [G, N] and outputs [N]");
+        if (indices->shape[0] != values->shape[0] || indices->shape[1] != values->shape[1] ||
+            out_indices->shape[0] != values->shape[1] || (out_values && out_values->shape[0] != values->shape[1]))
+            return fail(CTB_ERR_SHAPE, "shard results and outputs disagree in shape");
+        if (indices->dtype != CTB_INT64 || out_indices->dtype != CTB_INT64)
+            return fail(CTB_ERR_DTYPE, "indices must be int64");
+        if (out_values && out_values->dtype != values->dtype)
+            return fail(CTB_ERR_DTYPE, "combined values must have the shards' dtype");
+        if (values->dtype == CTB_BFLOAT16) return fail(CTB_ERR_DTYPE, "bfloat16 is not supported");
+        if (values->shape[0] > (int64_t(1) << 20)) return fail(CTB_ERR_SHAPE, "too many shards");
+        return minmax_combine(op, values, indices, d_row_offsets, out_values, out_indices,
+                              static_cast<cudaStream_t>(stream));
     });
 }
 

@@ -1,12 +1,18 @@
 """Row sharding across GPUs: one process per GPU (torch.distributed over NCCL for the plumbing),
 each holding a contiguous block of rows of a 2-D tensor.
 
-Only cross-shard reductions talk to other GPUs: a whole-tensor sum reduces each shard to one
-float64 partial on its GPU (ctb_sum_partial), all-gathers the partials (8 bytes per rank) and adds
-them in rank order on every GPU (ctb_sum_combine), so every rank holds the same, run-to-run
-identical float32 result. Row-wise work (elementwise ops with a broadcast row, per-row argmin) needs
-no communication; its outputs stay sharded. ctorch itself has no multi-GPU layer; this is the
-sharded form of its whole-tensor sum (src/ops/reduction_ops_cpu.cpp:463) and row-wise ops.
+Only cross-shard reductions talk to other GPUs:
+- a whole-tensor sum reduces each shard to one float64 partial on its GPU (ctb_sum_partial),
+  all-gathers the partials (8 bytes per rank) and adds them in rank order on every GPU
+  (ctb_sum_combine), so every rank holds the same, run-to-run identical float32 result;
+- a max/min over dim 0 (the rows) reduces each shard to its per-column (value, local row) pair
+  (ctb_reduce_index), all-gathers those (N values + N int64 indices per rank) and combines them in
+  rank order, shifting each shard's rows by its first global row (ctb_minmax_combine): the result
+  is the single-GPU reduction of the whole tensor, first NaN and first occurrence included.
+Row-wise work (elementwise ops with a broadcast row, per-row argmin, inner-dim reductions) and
+index_select over sharded indices need no communication; their outputs stay sharded. ctorch itself
+has no multi-GPU layer; these are the sharded forms of its whole-tensor sum
+(src/ops/reduction_ops_cpu.cpp:463), its max/min with indices (:236-297) and its row-wise ops.
 """
 from __future__ import annotations
 
@@ -113,3 +119,79 @@ def sharded_step_fused(x_local: torch.Tensor, r: torch.Tensor, summer: ShardedSu
     y, k, _ = chain_rows("sub", "mul", x_local, r, r, row_op="min", out_sum=summer.partial)
     s = summer.combine()
     return y, s, k
+
+
+def _local_minmax_cuda(op: str, local: torch.Tensor, values, indices, cache: dict) -> None:
+    from . import _capi as C
+    from .ops import _call, _scratch
+
+    code = C.MAX if op == "max" else C.MIN
+    vx = C.view(local)
+    need = C.lib.ctb_reduce_index_scratch_bytes(vx, 0)
+    if cache.get("need") != need:
+        cache["need"], cache["buf"] = need, _scratch(need, local.device)
+    buf = cache["buf"]
+    _call(C.lib.ctb_reduce_index(code, vx, C.view(values), C.view(indices), 0,
+                                 buf.data_ptr() if buf is not None else None, need,
+                                 C.stream_handle(local.device)), op)
+
+
+def _minmax_combine_cuda(op: str, all_values, all_indices, offsets, out_values, out_indices) -> None:
+    from . import _capi as C
+    from .ops import _call
+
+    code = C.MAX if op == "max" else C.MIN
+    _call(C.lib.ctb_minmax_combine(code, C.view(all_values), C.view(all_indices), offsets.data_ptr(),
+                                   C.view(out_values), C.view(out_indices),
+                                   C.stream_handle(all_values.device)), op)
+
+
+class ShardedColumnMinMax:
+    """max/min over dim 0 of a row-sharded 2-D tensor [total, N] (values and global row indices),
+    the same on every rank. Every rank must hold at least one row. Buffers are allocated once."""
+
+    def __init__(self, op: str, total: int, n_cols: int, dtype, device: torch.device, world: int,
+                 group=None, local_fn: Optional[Callable] = None, combine_fn: Optional[Callable] = None):
+        if op not in ("max", "min"):
+            raise ValueError("op must be 'max' or 'min'")
+        if total < world:
+            raise ValueError("every rank needs at least one row")
+        self.op, self.world, self.group = op, world, group
+        self.values = torch.empty(n_cols, dtype=dtype, device=device)
+        self.indices = torch.empty(n_cols, dtype=torch.int64, device=device)
+        # gathered flat (rank-major), viewed [world, N] for the combine
+        self._flat_values = torch.empty(world * n_cols, dtype=dtype, device=device)
+        self._flat_indices = torch.empty(world * n_cols, dtype=torch.int64, device=device)
+        self.all_values = self._flat_values.view(world, n_cols)
+        self.all_indices = self._flat_indices.view(world, n_cols)
+        self.offsets = torch.tensor([row_shard(total, r, world).start for r in range(world)],
+                                    dtype=torch.int64, device=device)
+        self.out_values = torch.empty(n_cols, dtype=dtype, device=device)
+        self.out_indices = torch.empty(n_cols, dtype=torch.int64, device=device)
+        self._cache: dict = {}
+        self.local_fn = local_fn or (lambda x, v, i: _local_minmax_cuda(op, x, v, i, self._cache))
+        self.combine_fn = combine_fn or (lambda av, ai, off, ov, oi: _minmax_combine_cuda(op, av, ai, off, ov, oi))
+
+    def __call__(self, local: torch.Tensor):
+        self.local_fn(local, self.values, self.indices)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self._flat_values, self.values, group=self.group)
+            dist.all_gather_into_tensor(self._flat_indices, self.indices, group=self.group)
+        else:
+            self.all_values.copy_(self.values.reshape(1, -1))
+            self.all_indices.copy_(self.indices.reshape(1, -1))
+        self.combine_fn(self.all_values, self.all_indices, self.offsets, self.out_values, self.out_indices)
+        return self.out_values, self.out_indices
+
+
+def sharded_index_select(table: torch.Tensor, indices: torch.Tensor, total: int, rank: int, world: int,
+                         select: Optional[Callable] = None) -> torch.Tensor:
+    """index_select(table, 0, indices) with the output rows sharded: the table is replicated and
+    each rank gathers the rows for its own contiguous slice of `indices` (indices[start:stop] of
+    the row_shard of `total` = len(indices)). No communication; the output stays sharded."""
+    from .ops import index_select
+
+    sh = row_shard(total, rank, world)
+    return (select or index_select)(table, 0, indices[sh.start:sh.stop])

@@ -219,6 +219,17 @@ CTB_API int ctb_sum_partial(const ctb_view* in, double* d_partial, void* scratch
  * once to out's dtype. Deterministic for a fixed n. */
 CTB_API int ctb_sum_combine(const double* d_partials, int n, const ctb_view* out, ctb_stream stream);
 
+/* Combine step of a row-sharded max/min over dim 0 (op = CTB_MAX / CTB_MIN): values [G, N] and
+ * int64 indices [G, N] hold the G shards' own results (row g = rank g's ctb_reduce_index output,
+ * indices local to its shard); d_row_offsets is a device int64 array of the G shards' first global
+ * rows. Writes out_indices [N] (global rows) and, unless NULL, out_values [N], combining the shards
+ * in rank order with ctorch's rule: the first NaN wins, otherwise the first occurrence of the
+ * extreme value (src/ops/reduction_ops_cpu.cpp:236-297). The result equals the single-GPU
+ * reduction of the whole tensor. No ctorch counterpart (ctorch has no multi-GPU layer). */
+CTB_API int ctb_minmax_combine(int op, const ctb_view* values, const ctb_view* indices,
+                               const int64_t* d_row_offsets, const ctb_view* out_values,
+                               const ctb_view* out_indices, ctb_stream stream);
+
 /* ---- synthetic inputs ---- */
 
 /* Fills a contiguous view with a counter-based pseudo-random sequence (splitmix64 of

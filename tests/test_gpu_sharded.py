@@ -1,0 +1,161 @@
+"""The row-sharded layer (ctorch_b200/sharded.py) on GPUs.
+
+- ctb_minmax_combine on one GPU, fed with the per-shard results of G emulated shards (each the
+  backend's own max/min over its rows), against the oracle's reduction of the whole tensor:
+  bit-exact, for every dtype, with NaNs and ties that straddle shard boundaries.
+- Two NCCL ranks on two GPUs (skipped with fewer): the sharded sum, the sharded column max/min
+  and the one-pass sharded step, each against the same computation on one GPU.
+"""
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+from helpers import assert_bitexact
+
+pytestmark = pytest.mark.gpu
+
+
+def _shard_inputs(dt, total, cols, seed):
+    rng = np.random.default_rng(seed)
+    dt = np.dtype(dt)
+    if dt.kind == "f":
+        x = (np.round(rng.standard_normal((total, cols)) * 2)).astype(dt)  # ties
+        x[::37, 1] = np.nan
+        x[5::41, 2] = -0.0
+    elif dt == np.bool_:
+        x = rng.integers(0, 2, (total, cols)).astype(np.bool_)
+    else:
+        x = rng.integers(-3, 4, (total, cols)).astype(dt)
+    x[:, 0] = x[0, 0] if dt != np.bool_ else True  # one tie down the whole column
+    return x
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.float64, np.int32, np.int64, np.bool_])
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_minmax_combine_of_emulated_shards(cuda_ok, oracle, dt, world):
+    import torch
+
+    import ctorch_b200 as cb
+    from ctorch_b200 import _capi as C
+    from ctorch_b200.sharded import row_shard
+
+    total, cols = 1003, 700
+    x = _shard_inputs(dt, total, cols, world)
+    tx = torch.from_numpy(x).cuda()
+    offs = torch.tensor([row_shard(total, r, world).start for r in range(world)], dtype=torch.int64, device="cuda")
+    for op, code in (("max", C.MAX), ("min", C.MIN)):
+        vals, idxs = [], []
+        for r in range(world):
+            sh = row_shard(total, r, world)
+            v, i = getattr(cb, op)(tx[sh.start:sh.stop], 0, False)
+            vals.append(v)
+            idxs.append(i)
+        av, ai = torch.stack(vals), torch.stack(idxs)
+        ov = torch.empty(cols, dtype=tx.dtype, device="cuda")
+        oi = torch.empty(cols, dtype=torch.int64, device="cuda")
+        rc = C.lib.ctb_minmax_combine(code, C.view(av), C.view(ai), offs.data_ptr(), C.view(ov), C.view(oi),
+                                      C.stream_handle())
+        assert rc == C.OK, C.last_error()
+        rv, ri = oracle.reduce_idx(op, x, 0, False)
+        assert_bitexact(ov.cpu().numpy(), rv, f"{op} values, {world} shards")
+        assert_bitexact(oi.cpu().numpy(), ri, f"{op} indices, {world} shards")
+        # indices only
+        oi2 = torch.empty(cols, dtype=torch.int64, device="cuda")
+        rc = C.lib.ctb_minmax_combine(code, C.view(av), C.view(ai), offs.data_ptr(), None, C.view(oi2),
+                                      C.stream_handle())
+        assert rc == C.OK, C.last_error()
+        assert torch.equal(oi2, oi)
+
+
+def test_minmax_combine_rejects_bad_arguments(cuda_ok):
+    import torch
+
+    from ctorch_b200 import _capi as C
+
+    av = torch.zeros(2, 5, device="cuda")
+    ai = torch.zeros(2, 5, dtype=torch.int64, device="cuda")
+    offs = torch.zeros(2, dtype=torch.int64, device="cuda")
+    oi = torch.empty(5, dtype=torch.int64, device="cuda")
+    assert C.lib.ctb_minmax_combine(C.SUM, C.view(av), C.view(ai), offs.data_ptr(), None, C.view(oi),
+                                    C.stream_handle()) == C.ERR_ARGUMENT
+    bad = torch.empty(4, dtype=torch.int64, device="cuda")
+    assert C.lib.ctb_minmax_combine(C.MAX, C.view(av), C.view(ai), offs.data_ptr(), None, C.view(bad),
+                                    C.stream_handle()) == C.ERR_SHAPE
+    ai32 = torch.zeros(2, 5, dtype=torch.int32, device="cuda")
+    assert C.lib.ctb_minmax_combine(C.MAX, C.view(av), C.view(ai32), offs.data_ptr(), None, C.view(oi),
+                                    C.stream_handle()) == C.ERR_DTYPE
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _nccl_worker(rank, world, port, results):
+    import torch
+    import torch.distributed as dist
+
+    import ctorch_b200 as cb
+    from ctorch_b200.sharded import ShardedColumnMinMax, ShardedSum, row_shard, sharded_step_fused
+    from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        total, cols = 4099, 2048
+        full = device_fill(torch.empty(total, cols, device=dev), NORMAL, 9, 0, 0.0, 1.0)
+        r = device_fill(torch.empty(1, cols, device=dev), UNIFORM, 9, 1, -1.0, 1.0)
+        sh = row_shard(total, rank, world)
+        local = full[sh.start:sh.stop]
+        summer = ShardedSum(dev, world)
+        y, s, k = sharded_step_fused(local, r, summer)
+        mx = ShardedColumnMinMax("max", total, cols, torch.float32, dev, world)
+        mv, mi = mx(local)
+        mn = ShardedColumnMinMax("min", total, cols, torch.float32, dev, world)
+        nv, ni = mn(local)
+        torch.cuda.synchronize()
+        out = {"s": float(s), "k": k.cpu(), "y_sum": float(y.double().sum()), "mv": mv.cpu(), "mi": mi.cpu(),
+               "nv": nv.cpu(), "ni": ni.cpu()}
+        if rank == 0:  # the whole tensor on one GPU
+            y1 = cb.binary_chain("sub", "mul", full, r, r)
+            out["ref"] = {"s": float(cb.sum(y1)), "k": cb.argmin(y1, 1).cpu(), "max": cb.max(full, 0, False),
+                          "min": cb.min(full, 0, False)}
+            out["ref"]["max"] = (out["ref"]["max"].values.cpu(), out["ref"]["max"].indices.cpu())
+            out["ref"]["min"] = (out["ref"]["min"].values.cpu(), out["ref"]["min"].indices.cpu())
+        results[rank] = out
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+def test_sharded_layer_on_two_gpus(cuda_ok):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), results), nprocs=world, start_method="spawn",
+                       join=True)
+    ref = results[0]["ref"]
+    ks = torch.cat([results[r]["k"] for r in range(world)])
+    assert torch.equal(ks, ref["k"])
+    for r in range(world):
+        o = results[r]
+        assert o["s"] == results[0]["s"]  # every rank holds the same sum
+        assert abs(o["s"] - ref["s"]) <= 1e-5 * max(1.0, abs(ref["s"]))
+        assert torch.equal(o["mv"], ref["max"][0]) and torch.equal(o["mi"], ref["max"][1])
+        assert torch.equal(o["nv"], ref["min"][0]) and torch.equal(o["ni"], ref["min"][1])

@@ -1,7 +1,7 @@
 """Host logic of the row-sharded layer (ctorch_b200/sharded.py) on CPU: the row partition, and
 the partial -> all-gather -> rank-order combine of a whole-tensor sum, run as two gloo ranks.
 The per-shard partial and the combine are injected as CPU functions here; on GPUs they are
-ctb_sum_partial / ctb_sum_combine (tests/test_gpu_sharded.py)."""
+ctb_sum_partial / ctb_sum_combine and ctb_reduce_index / ctb_minmax_combine (tests/test_gpu_sharded.py)."""
 import os
 import socket
 
@@ -73,3 +73,104 @@ def test_sharded_sum_two_gloo_ranks():
     s1, g1, _ = results[1]
     assert s0 == s1 == g0[0] == g0[1]  # every rank holds the same value
     assert abs(s0 - ref) <= 1e-5 * max(1.0, abs(ref))
+
+
+def _local_minmax_oracle(op):
+    from oracle.oracle import oracle
+
+    O = oracle()
+
+    def fn(local, values, indices):
+        v, i = O.reduce_idx(op, local.numpy(), 0, False)
+        values.copy_(torch.from_numpy(v))
+        indices.copy_(torch.from_numpy(i))
+
+    return fn
+
+
+def _better(op, v, i, bv, bi):
+    """ctorch's max/min-with-index rule (src/ops/reduction_ops_cpu.cpp:236-297), restated."""
+    import math
+
+    if bv is None:
+        return True
+    if isinstance(v, float) and math.isnan(v):
+        return not (isinstance(bv, float) and math.isnan(bv)) or i < bi
+    if isinstance(bv, float) and math.isnan(bv):
+        return False
+    if (v > bv) if op == "max" else (v < bv):
+        return True
+    return v == bv and i < bi
+
+
+def _minmax_combine_cpu(op):
+    def fn(all_values, all_indices, offsets, out_values, out_indices):
+        for n in range(all_values.shape[1]):
+            bv = bi = None
+            for g in range(all_values.shape[0]):  # rank order
+                v = all_values[g, n].item()
+                i = int(offsets[g]) + int(all_indices[g, n])
+                if _better(op, v, i, bv, bi):
+                    bv, bi = v, i
+            out_values[n] = bv
+            out_indices[n] = bi
+
+    return fn
+
+
+def _minmax_worker(rank, world, port, total, cols, results):
+    import numpy as np
+
+    from ctorch_b200.sharded import ShardedColumnMinMax
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(5)
+        full = np.round(rng.standard_normal((total, cols)) * 2).astype(np.float32)  # many ties
+        full[::17, 3] = np.nan
+        full[:, 5] = 7.0  # a column that is one tie all the way down, across the shard boundary
+        sh = row_shard(total, rank, world)
+        out = {}
+        for op in ("max", "min"):
+            mm = ShardedColumnMinMax(op, total, cols, torch.float32, torch.device("cpu"), world,
+                                     local_fn=_local_minmax_oracle(op), combine_fn=_minmax_combine_cpu(op))
+            v, i = mm(torch.from_numpy(full[sh.start:sh.stop]).contiguous())
+            out[op] = (v.numpy().copy(), i.numpy().copy())
+        results[rank] = (out, full)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_column_minmax_two_gloo_ranks():
+    """Per-shard max/min with local indices, all-gathered and combined in rank order with the
+    shard offsets, equals the oracle's reduction of the whole tensor on every rank."""
+    import numpy as np
+
+    from oracle.oracle import oracle
+
+    world, total, cols = 2, 301, 9
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_minmax_worker, args=(world, _free_port(), total, cols, results), nprocs=world,
+                       start_method="spawn", join=True)
+    full = results[0][1]
+    O = oracle()
+    for op in ("max", "min"):
+        rv, ri = O.reduce_idx(op, full, 0, False)
+        for rank in range(world):
+            v, i = results[rank][0][op]
+            assert np.array_equal(i, ri), (op, rank, i, ri)
+            assert np.array_equal(np.isnan(v), np.isnan(rv))
+            assert np.array_equal(v[~np.isnan(v)], rv[~np.isnan(rv)])
+    assert results[0][0]["max"][1][5] == 0  # the all-tie column: first row
+
+
+def test_sharded_index_select_covers_all_rows():
+    from ctorch_b200.sharded import sharded_index_select
+
+    table = torch.arange(40, dtype=torch.float32).reshape(10, 4)
+    idx = torch.tensor([3, 1, 4, 1, 5, 9, 2, 6, 5])
+    parts = [sharded_index_select(table, idx, len(idx), r, 4, select=torch.index_select) for r in range(4)]
+    assert torch.equal(torch.cat(parts), table[idx])
