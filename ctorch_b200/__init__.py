@@ -17,8 +17,10 @@ from .ops import (  # noqa: F401
     argmin,
     binary_chain,
     binary_unary,
-    chain_rows,
     broadcast_shape,
+    cast,
+    chain_rows,
+    contiguous,
     div,
     div_,
     exp,

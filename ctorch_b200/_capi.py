@@ -64,6 +64,7 @@ def _load() -> ctypes.CDLL:
         "ctb_binary": (i32, [i32, P, P, P, vp]),
         "ctb_binary_chain": (i32, [i32, i32, P, P, P, ctypes.c_int32, P, vp]),
         "ctb_unary": (i32, [i32, P, P, vp]),
+        "ctb_cast": (i32, [P, P, vp]),
         "ctb_binary_unary": (i32, [i32, i32, P, P, P, vp]),
         "ctb_reduce_scratch_bytes": (sz, [i32, P, P, u32]),
         "ctb_reduce": (i32, [i32, P, P, u32, vp, sz, vp]),

@@ -31,6 +31,7 @@ int minmax_dispatch(int op, const ctb_view* in, const ctb_view* values, const ct
 int sum_partial_dispatch(const ctb_view* in, double* d_partial, void* scratch, size_t sb,
                          cudaStream_t st, size_t* need_only);
 int sum_combine(const double* parts, int n, const ctb_view* out, cudaStream_t st);
+int cast_dispatch(const ctb_view* in, const ctb_view* out, cudaStream_t st);
 int minmax_combine(int op, const ctb_view* values, const ctb_view* indices, const int64_t* d_offsets,
                    const ctb_view* out_values, const ctb_view* out_indices, cudaStream_t st);
 int index_select_dispatch(const ctb_view* src, int dim, const ctb_view* idx, const ctb_view* out,
@@ -257,6 +258,20 @@ int ctb_unary(int op, const ctb_view* in, const ctb_view* out, ctb_stream stream
         if (!int_ok && (dt == CTB_INT32 || dt == CTB_INT64))
             return fail(CTB_ERR_DTYPE, "only float32/float64 inputs are supported");
         return unary_dispatch(op, in, out, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int ctb_cast(const ctb_view* in, const ctb_view* out, ctb_stream stream) {
+    return guarded([&]() -> int {
+        t_error.clear();
+        if (int rc = check_views({in, out})) return rc;
+        // src/ops/cast_cpu.cpp:62-90
+        if (in->dtype == CTB_BFLOAT16) return fail(CTB_ERR_DTYPE, "ctorch: cast from bfloat16 not supported");
+        if (out->dtype == CTB_BFLOAT16) return fail(CTB_ERR_DTYPE, "ctorch: cast to bfloat16 not supported");
+        if (in->ndim != out->ndim) return fail(CTB_ERR_SHAPE, "cast output shape must equal the input shape");
+        for (int d = 0; d < in->ndim; ++d)
+            if (in->shape[d] != out->shape[d]) return fail(CTB_ERR_SHAPE, "cast output shape must equal the input shape");
+        return cast_dispatch(in, out, static_cast<cudaStream_t>(stream));
     });
 }
 

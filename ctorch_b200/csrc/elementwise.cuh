@@ -29,12 +29,18 @@ constexpr int kRowDivMinBlocks = 3;
 
 struct NoIn {};
 
+// Elements per pack: one 16-byte chunk of the narrowest operand, capped so the widest operand's
+// pack stays within 32 bytes (a bool <- int64 cast takes 4 elements, not 16).
 template <class O, class I0, class I1, class I2, int NIN> constexpr int ew_vec() {
-    int m = sizeof(O);
+    int m = sizeof(O), w = sizeof(O);
     if ((int)sizeof(I0) < m) m = sizeof(I0);
+    if ((int)sizeof(I0) > w) w = sizeof(I0);
     if (NIN > 1 && (int)sizeof(I1) < m) m = sizeof(I1);
+    if (NIN > 1 && (int)sizeof(I1) > w) w = sizeof(I1);
     if (NIN > 2 && (int)sizeof(I2) < m) m = sizeof(I2);
-    return 16 / m;
+    if (NIN > 2 && (int)sizeof(I2) > w) w = sizeof(I2);
+    const int v = 16 / m;
+    return v * w > 32 ? 32 / w : v;
 }
 
 template <class Fn, class O, class I0, class I1, class I2, int NIN>

@@ -21,6 +21,7 @@
 #include "cuda/device_guard.h"
 #include "ops/reduction.h"
 
+#include "b200_cast.h"
 #include "ctb/ctb.h"
 
 #include <cuda_runtime.h>
@@ -170,6 +171,24 @@ void index_select_cuda(const Tensor& src, int dim, const Tensor& indices, Tensor
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------- cast / contiguous (b200_cast.h)
+
+namespace b200 {
+
+Tensor cast_cuda(const Tensor& t, dtype target) {
+    if (!t.device().is_cuda()) throw DeviceError("ctorch::b200::cast_cuda: tensor not on a CUDA device");
+    if (t.dtype() == target && t.is_contiguous() && t.offset() == 0) return t;
+    Tensor out(t.shape(), target, t.device());
+    cuda::DeviceGuard guard(t.device().index);
+    const ctb_view vi = view_of(t), vo = view_of(out);
+    check(ctb_cast(&vi, &vo, kLegacyStream), "cast");
+    return out;
+}
+
+Tensor contiguous_cuda(const Tensor& t) { return cast_cuda(t, t.dtype()); }
+
+}  // namespace b200
 
 extern "C" void ctorch_register_cuda_binary_ops() {
     dispatch::register_op<op::AddOp>(Device::Kind::CUDA, &binary_cuda<CTB_ADD>);

@@ -10,6 +10,9 @@
 #include "ctorch/ops/reduction.h"
 #include "ctorch/tensor.h"
 
+#include "b200_cast.h"
+#include "ops/cast_cpu.h"
+
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -222,6 +225,24 @@ int main(int argc, char** argv) {
     const int64_t bv = 300;
     std::memcpy(bad.storage().data(), &bv, sizeof(bv));
     report(throws<ShapeError>([&] { index_select(X.to(gpu), 0, bad.to(gpu)); }), "index_select out of range throws");
+
+    // device-side cast and contiguous (b200_cast.h) vs ctorch's CPU cast
+    {
+        const dtype dts[] = {dtype::float32, dtype::float64, dtype::int32, dtype::int64, dtype::bool_};
+        for (dtype from : dts) {
+            Tensor src = make({37, 53}, from);
+            Tensor view_g = src.to(gpu).permute(std::vector<int64_t>{1, 0});
+            Tensor view_c = src.permute(std::vector<int64_t>{1, 0});
+            for (dtype to : dts) {
+                Tensor g = b200::cast_cuda(view_g, to);
+                report(g.is_contiguous() && same_bits(g, ops::cast_cpu(view_c.contiguous(), to)),
+                       std::string("cast ") + std::to_string(static_cast<int>(from)) + "->" +
+                           std::to_string(static_cast<int>(to)));
+            }
+            report(same_bits(b200::contiguous_cuda(view_g), view_c.contiguous()), "contiguous_cuda");
+        }
+        report(throws<DTypeError>([&] { b200::cast_cuda(X.to(gpu), dtype::bfloat16); }), "cast to bfloat16 throws");
+    }
 
     std::printf("plugin_check: %d passed, %d failed\n", g_pass, g_fail);
     return g_fail ? 1 : 0;

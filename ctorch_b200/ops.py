@@ -232,6 +232,29 @@ def _unary(op: int, x: torch.Tensor, name: str) -> torch.Tensor:
     return out
 
 
+def cast(x: torch.Tensor, dtype) -> torch.Tensor:
+    """x converted to `dtype` (a new contiguous tensor; x itself when the dtype already matches
+    and x is contiguous), with ctorch's cast semantics (src/ops/cast_cpu.cpp:21-90) computed on
+    the GPU. This is the device-side cast that ctorch's CUDA promotion does through the host
+    (src/ops/binary_ops_cpu.cpp:154-184), and it also takes non-contiguous views."""
+    dev = _cuda("cast", x)
+    if dtype not in C.CODE_OF_TORCH or x.dtype not in C.CODE_OF_TORCH:
+        raise DTypeError(f"ctorch: cast from {x.dtype} to {dtype} is not supported")
+    if dtype == x.dtype and x.is_contiguous():
+        return x
+    out = torch.empty(x.shape, dtype=dtype, device=dev)
+    with torch.cuda.device(dev):
+        _call(C.lib.ctb_cast(C.view(x), C.view(out), C.stream_handle(dev)), "cast")
+    return out
+
+
+def contiguous(x: torch.Tensor) -> torch.Tensor:
+    """A contiguous copy of a strided CUDA view, made on the device (ctorch's Tensor::contiguous,
+    src/tensor.cpp:239-254, materialises strided tensors on the CPU only); x itself when it is
+    already contiguous."""
+    return cast(x, x.dtype)
+
+
 def neg(x):
     return _unary(C.NEG, x, "neg")
 

@@ -106,6 +106,17 @@ CTB_API int ctb_wait_timeouts(uint64_t* count);
 CTB_API int ctb_binary(int op, const ctb_view* a, const ctb_view* b, const ctb_view* out,
                ctb_stream stream);
 
+/* out = in converted to out's dtype, elementwise; out has in's shape and any strides. The
+ * conversions of ctorch's cast (src/ops/cast_cpu.cpp:21-90): static_cast, bool read as 0/1, any
+ * nonzero (NaN included) written to bool as true, float -> integer truncated toward zero. A NaN or
+ * out-of-range float -> integer is undefined behaviour in ctorch (its x86 build gives the integer
+ * minimum); here it saturates and NaN gives 0. With out's dtype equal to in's and out contiguous
+ * this is a strided -> contiguous copy. It stands in for the host round trip of ctorch's CUDA
+ * promotion (`maybe_cast`, src/ops/binary_ops_cpu.cpp:154-184, whose comment asks for a cast_cuda
+ * kernel) and for the CPU-only strided materialisation of Tensor::contiguous()
+ * (src/tensor.cpp:239-254). bfloat16 gives CTB_ERR_DTYPE. */
+CTB_API int ctb_cast(const ctb_view* in, const ctb_view* out, ctb_stream stream);
+
 /* out = op2(op1(a, b), c) in one pass, with the intermediate rounded to `mid_dtype` exactly as the
  * unfused pair of ctb_binary calls would round it (so results are bit-identical to the eager
  * sequence). mid_dtype must equal promote_types(a, b); out's dtype must equal

@@ -304,6 +304,54 @@ int orc_unary(int op, const orc_view* in, const orc_view* out) {
     return ORC_OK;
 }
 
+/* ---------------------------------------------------------------------- cast */
+
+/* src/ops/cast_cpu.cpp:21-90: out = static_cast<out dtype>(in) elementwise over the same shape,
+ * bool read as 0/1 (the static_cast loads above) and written as (value != 0). */
+int orc_cast(const orc_view* in, const orc_view* out) {
+    if (in->dtype == ORC_BF16 || out->dtype == ORC_BF16) return ORC_ERR_DTYPE;
+    if (in->ndim != out->ndim) return ORC_ERR_SHAPE;
+    for (int d = 0; d < in->ndim; ++d)
+        if (in->shape[d] != out->shape[d]) return ORC_ERR_SHAPE;
+    const int r = out->ndim;
+    const int64_t n = view_numel(out);
+    int64_t idx[ORC_MAX_DIMS] = {0};
+    int64_t io = 0, oo = 0;
+    const size_t es = dtype_size(out->dtype);
+    for (int64_t i = 0; i < n; ++i) {
+        char* po = (char*)out->data + oo * (int64_t)es;
+        switch (out->dtype) {
+        case ORC_F32: *(float*)po = ld_f32(in, io); break;
+        case ORC_F64: *(double*)po = ld_f64(in, io); break;
+        case ORC_I32: *(int32_t*)po = ld_i32(in, io); break;
+        case ORC_I64: *(int64_t*)po = ld_i64(in, io); break;
+        case ORC_BOOL: {
+            const char* pi = elem_ptr(in, io);
+            int nz = 0;
+            switch (in->dtype) {
+            case ORC_F32: nz = *(const float*)pi != 0.0f; break;
+            case ORC_F64: nz = *(const double*)pi != 0.0; break;
+            case ORC_I32: nz = *(const int32_t*)pi != 0; break;
+            case ORC_I64: nz = *(const int64_t*)pi != 0; break;
+            case ORC_BOOL: nz = *(const uint8_t*)pi != 0; break;
+            }
+            *(uint8_t*)po = (uint8_t)nz;
+            break;
+        }
+        }
+        for (int d = r - 1; d >= 0; --d) {
+            ++idx[d];
+            io += in->strides[d];
+            oo += out->strides[d];
+            if (idx[d] < out->shape[d]) break;
+            idx[d] = 0;
+            io -= in->strides[d] * out->shape[d];
+            oo -= out->strides[d] * out->shape[d];
+        }
+    }
+    return ORC_OK;
+}
+
 /* ---------------------------------------------------------------- reductions */
 
 typedef struct {

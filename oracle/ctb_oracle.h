@@ -53,6 +53,9 @@ int orc_binary(int op, const orc_view* a, const orc_view* b, const orc_view* out
 /* out = op(in), same shape and dtype. */
 int orc_unary(int op, const orc_view* in, const orc_view* out);
 
+/* out = in converted to out's dtype (same shape, any strides). */
+int orc_cast(const orc_view* in, const orc_view* out);
+
 /* Multi-axis reduction: bit d of reduce_mask marks input dim d as reduced. out has either the
  * keepdim shape (rank == in rank) or the kept dims only. */
 int orc_reduce(int op, const orc_view* in, const orc_view* out, uint32_t reduce_mask);

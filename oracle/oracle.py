@@ -104,10 +104,11 @@ class Oracle:
         P = ctypes.POINTER(OrcView)
         lib.orc_binary.argtypes = [ctypes.c_int, P, P, P]
         lib.orc_unary.argtypes = [ctypes.c_int, P, P]
+        lib.orc_cast.argtypes = [P, P]
         lib.orc_reduce.argtypes = [ctypes.c_int, P, P, ctypes.c_uint32]
         lib.orc_reduce_idx.argtypes = [ctypes.c_int, P, P, P, ctypes.c_int]
         lib.orc_index_select.argtypes = [P, ctypes.c_int, P, P, ctypes.POINTER(ctypes.c_int64)]
-        for f in ("orc_binary", "orc_unary", "orc_reduce", "orc_reduce_idx", "orc_index_select"):
+        for f in ("orc_binary", "orc_unary", "orc_cast", "orc_reduce", "orc_reduce_idx", "orc_index_select"):
             getattr(lib, f).restype = ctypes.c_int
         self.lib = lib
 
@@ -126,6 +127,11 @@ class Oracle:
     def unary(self, op: str, x: np.ndarray) -> np.ndarray:
         out = np.empty(x.shape, dtype=x.dtype)
         self._check(self.lib.orc_unary(UNARY_OPS[op], make_view(x), make_view(out)), op)
+        return out
+
+    def cast(self, x: np.ndarray, dtype) -> np.ndarray:
+        out = np.empty(x.shape, dtype=dtype)
+        self._check(self.lib.orc_cast(make_view(x), make_view(out)), "cast")
         return out
 
     @staticmethod
@@ -225,6 +231,8 @@ class Ref:
         lib.ref_reduce_idx.restype = vp
         lib.ref_arg.argtypes = [ctypes.c_int, vp, ctypes.c_int64, ctypes.c_int, ip]
         lib.ref_arg.restype = vp
+        lib.ref_cast.argtypes = [vp, ctypes.c_int, ip]
+        lib.ref_cast.restype = vp
         lib.ref_index_select.argtypes = [vp, ctypes.c_int, vp, ip]
         lib.ref_index_select.restype = vp
         self.lib = lib
@@ -241,6 +249,10 @@ class Ref:
         h = self.lib.ref_tensor_from(code_of(arr.dtype), arr.ndim, shape,
                                      arr.__array_interface__["data"][0], ctypes.byref(err))
         return self._wrap(h, err)
+
+    def cast(self, a, dtype):
+        err = ctypes.c_int(0)
+        return self._wrap(self.lib.ref_cast(a.h, code_of(np.dtype(dtype)), ctypes.byref(err)), err)
 
     def binary(self, op, a, b):
         err = ctypes.c_int(0)

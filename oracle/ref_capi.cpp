@@ -4,12 +4,14 @@
 // TEST INFRASTRUCTURE ONLY. The tests use it to pin the C restatement (ctb_oracle.c) bit-for-bit
 // against ctorch itself, and bench.py's reference arm / CPU-baseline leg time ctorch's public
 // front-doors through it. Every op goes through the public free functions declared in
-// include/ctorch/ops/{elementwise,reduction,indexing}.h, i.e. ctorch's stock CPU code path.
+// include/ctorch/ops/{elementwise,reduction,indexing}.h, i.e. ctorch's stock CPU code path; the
+// one exception is ref_cast, ctorch's internal cast helper (no public front-door casts).
 #include "ctorch/errors.h"
 #include "ctorch/ops/elementwise.h"
 #include "ctorch/ops/indexing.h"
 #include "ctorch/ops/reduction.h"
 #include "ctorch/tensor.h"
+#include "ops/cast_cpu.h"
 
 #include <cstdint>
 #include <cstring>
@@ -115,6 +117,14 @@ void* ref_select(void* h, int dim, int64_t index, int* err) {
 void* ref_reshape(void* h, int n, const int64_t* shape, int* err) {
     return guarded(err, [&]() -> void* {
         return box(un(h).reshape(std::vector<std::int64_t>(shape, shape + n)));
+    });
+}
+
+// ctorch's dtype cast (src/ops/cast_cpu.cpp:62-90), the one its CUDA promotion round trip runs
+// (src/ops/binary_ops_cpu.cpp:154-184). It is an in-library helper, not a public front-door.
+void* ref_cast(void* h, int dt, int* err) {
+    return guarded(err, [&]() -> void* {
+        return box(ctorch::ops::cast_cpu(un(h), static_cast<ctorch::dtype>(dt)));
     });
 }
 
