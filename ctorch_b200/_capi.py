@@ -78,6 +78,12 @@ def _load() -> ctypes.CDLL:
         "ctb_sum_partial": (i32, [P, vp, vp, sz, vp]),
         "ctb_sum_combine": (i32, [vp, i32, P, vp]),
         "ctb_minmax_combine": (i32, [i32, P, P, vp, P, P, vp]),
+        "ctb_peer_workspace_bytes": (sz, []),
+        "ctb_peer_alloc": (i32, [ctypes.POINTER(vp), vp]),
+        "ctb_peer_open": (i32, [vp, ctypes.POINTER(vp)]),
+        "ctb_peer_close": (i32, [vp]),
+        "ctb_peer_free": (i32, [vp]),
+        "ctb_chain_rows_allsum": (i32, [i32, i32, P, P, P, P, i32, P, vp, vp, i32, i32, u64, P, vp, u64, vp]),
         "ctb_fill_random": (i32, [P, i32, u64, u64, i64, ctypes.c_double, ctypes.c_double, vp]),
         "ctb_debug_plan_elementwise": (i32, [P, ctypes.POINTER(P), i32, i32, ctypes.c_char_p, i32,
                                              ctypes.POINTER(ctypes.c_int),

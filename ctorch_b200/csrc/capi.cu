@@ -10,6 +10,7 @@
 #include <tuple>
 
 #include "common.cuh"
+#include "peer.cuh"
 #include "plan.cuh"
 
 namespace ctb {
@@ -31,6 +32,11 @@ int minmax_dispatch(int op, const ctb_view* in, const ctb_view* values, const ct
 int sum_partial_dispatch(const ctb_view* in, double* d_partial, void* scratch, size_t sb,
                          cudaStream_t st, size_t* need_only);
 int sum_combine(const double* parts, int n, const ctb_view* out, cudaStream_t st);
+int fused_rows_allsum(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                      const ctb_view* y, int row_op, const ctb_view* idx, PeerWorkspace* const* d_peers,
+                      int rank, int world, uint64_t epoch, const ctb_view* out_sum, double* d_parts,
+                      uint64_t timeout_ns, unsigned long long* timeouts, PeerWorkspace* my_ws, cudaStream_t st);
+unsigned long long* wait_timeout_counter();
 int cast_dispatch(const ctb_view* in, const ctb_view* out, cudaStream_t st);
 int minmax_combine(int op, const ctb_view* values, const ctb_view* indices, const int64_t* d_offsets,
                    const ctb_view* out_values, const ctb_view* out_indices, cudaStream_t st);
@@ -427,6 +433,33 @@ size_t ctb_sum_partial_scratch_bytes(const ctb_view* in) {
         return sum_partial_dispatch(in, &dummy, nullptr, 0, nullptr, &need);
     });
     return need;
+}
+
+int ctb_chain_rows_allsum(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                          const ctb_view* y, int row_op, const ctb_view* row_index, void* const* d_peer_workspaces,
+                          void* d_my_workspace, int rank, int world, uint64_t epoch, const ctb_view* out_sum,
+                          double* d_rank_partials, uint64_t timeout_ns, ctb_stream stream) {
+    return guarded([&]() -> int {
+        t_error.clear();
+        if (int rc = check_views({a, b, c, out_sum})) return rc;
+        if (y)
+            if (int rc = check_views({y})) return rc;
+        if (row_index)
+            if (int rc = check_views({row_index})) return rc;
+        if (!d_peer_workspaces || !d_my_workspace) return fail(CTB_ERR_ARGUMENT, "null workspace");
+        if (world < 1 || world > kPeerMaxRanks || rank < 0 || rank >= world)
+            return fail(CTB_ERR_ARGUMENT, "rank/world out of range (world <= " + std::to_string(kPeerMaxRanks) + ")");
+        if (epoch == 0) return fail(CTB_ERR_ARGUMENT, "epoch must start at 1 and grow by one per call");
+        if (out_sum->dtype != CTB_FLOAT32 && out_sum->dtype != CTB_FLOAT64)
+            return fail(CTB_ERR_DTYPE, "the sum must be float32 or float64");
+        if (view_numel(out_sum) != 1) return fail(CTB_ERR_SHAPE, "the sum output must hold one element");
+        unsigned long long* counter = wait_timeout_counter();
+        if (!counter) return fail(CTB_ERR_CUDA, "device timeout counter unavailable");
+        return fused_rows_allsum(op1, op2, a, b, c, y, row_op, row_index,
+                                 reinterpret_cast<PeerWorkspace* const*>(d_peer_workspaces), rank, world, epoch,
+                                 out_sum, d_rank_partials, timeout_ns ? timeout_ns : 1000000000ull, counter,
+                                 static_cast<PeerWorkspace*>(d_my_workspace), static_cast<cudaStream_t>(stream));
+    });
 }
 
 int ctb_sum_partial(const ctb_view* in, double* d_partial, void* scratch, size_t scratch_bytes,

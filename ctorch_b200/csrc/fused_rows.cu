@@ -9,9 +9,19 @@
 // lanes' (value, index) states are combined by warp shuffles with the full tie/NaN rule of
 // src/ops/reduction_functors.h:55-110. Reads a once and writes y once: the eager sequence
 // (chain, then sum, then argmin) reads y twice more.
+//
+// Across GPUs (ctb_chain_rows_allsum): the last CTA to finish (a ticket in this rank's peer
+// workspace, reset by that CTA) also sums the per-CTA partials into the rank's partial, stores it
+// over NVLink into slot `rank` of every rank's workspace (an IPC mapping of each peer's memory)
+// with the call's epoch, waits until every rank's slot in its own workspace carries that epoch,
+// and adds the slots in rank order: the whole-job sum, on every rank, from the one launch. The
+// waits are bounded in time; a wait that runs out is counted (ctb_wait_timeouts) and the sum is
+// left unwritten.
 #include <limits>
 
+#include "async_copy.cuh"
 #include "common.cuh"
+#include "peer.cuh"
 #include "plan.cuh"
 
 namespace ctb {
@@ -28,7 +38,91 @@ struct FusedRowsArgs {
     int b_bcast, c_bcast;  // 1: b/c is a 0-d scalar (stride 0 along the row)
     int c_is_b;
     int is_max;
+    // cross-GPU sum (ctb_chain_rows_allsum); peers == nullptr otherwise
+    PeerWorkspace* const* peers;  // device array of every rank's workspace (this rank's own at [rank])
+    int rank, world;
+    uint64_t epoch;
+    uint64_t timeout_ns;
+    void* out_sum;         // 0-d float32/float64
+    int out_sum_dtype;
+    double* out_parts;     // [world] rank partials, may be null
+    unsigned long long* timeouts;
 };
+
+// Sum of n per-CTA partials by one 256-thread block: thread t adds partials t, t + 256, ... in
+// order, then a fixed tree (warp shuffles, then the 8 warps' sums in order). Result in thread 0.
+// The shape depends only on n, so the sum is run-to-run identical, and the same on the one-GPU
+// (fused_rows_combine) and cross-GPU (last CTA) paths.
+__device__ __forceinline__ double tree_sum_256(const double* partials, int n, double* sm8) {
+    double s = 0.0;
+    for (int i = threadIdx.x; i < n; i += 256) s = __dadd_rn(s, __ldcg(partials + i));
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, m));
+    if ((threadIdx.x & 31) == 0) sm8[threadIdx.x >> 5] = s;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x == 0)
+        for (int w = 0; w < 8; ++w) t = __dadd_rn(t, sm8[w]);
+    return t;
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Cross-GPU epilogue, run by every thread of the last CTA of this rank's launch (256 threads).
+__device__ void allsum_epilogue(const FusedRowsArgs& p) {
+    __shared__ double sm8[8];
+    __shared__ double rank_sum[kPeerMaxRanks];
+    __shared__ int ok_all;
+    const double mine = tree_sum_256(p.partials, static_cast<int>(gridDim.x), sm8);
+    __shared__ double mine_sh;
+    if (threadIdx.x == 0) {
+        mine_sh = mine;
+        ok_all = 1;
+    }
+    __syncthreads();
+    const int g = threadIdx.x;
+    if (g < p.world) {
+        // publish: value, then (after a system-scope fence) the epoch that marks it valid
+        PeerSlot* dst = &p.peers[g]->slots[p.rank];
+        *reinterpret_cast<volatile double*>(&dst->value) = mine_sh;
+        __threadfence_system();
+        st_release_sys(&dst->epoch, p.epoch);
+    }
+    if (g < p.world) {
+        // wait for rank g's value in this rank's own workspace
+        PeerSlot* src = &p.peers[p.rank]->slots[g];
+        bool ok = ld_acquire_sys(&src->epoch) >= p.epoch;
+        if (!ok) {
+            const uint64_t t0 = global_ns();
+            while (!(ok = ld_acquire_sys(&src->epoch) >= p.epoch))
+                if (global_ns() - t0 > p.timeout_ns) break;
+        }
+        if (ok) rank_sum[g] = *reinterpret_cast<volatile const double*>(&src->value);
+        else atomicExch(&ok_all, 0);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (!ok_all) {
+            note_timeout(p.timeouts);
+            return;
+        }
+        double s = 0.0;
+        for (int r = 0; r < p.world; ++r) {  // rank order
+            s = __dadd_rn(s, rank_sum[r]);
+            if (p.out_parts) p.out_parts[r] = rank_sum[r];
+        }
+        if (p.out_sum_dtype == CTB_FLOAT32) *static_cast<float*>(p.out_sum) = static_cast<float>(s);
+        else *static_cast<double*>(p.out_sum) = s;
+    }
+}
 
 template <class T> __device__ __forceinline__ T extreme_ident(bool is_max) {
     return is_max ? -std::numeric_limits<T>::infinity() : std::numeric_limits<T>::infinity();
@@ -154,14 +248,29 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
             for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s = __dadd_rn(s, sm[w]);
             p.partials[blockIdx.x] = s;
         }
+        if (p.peers) {
+            // the last CTA to finish takes the cross-GPU epilogue
+            __shared__ int last;
+            if (threadIdx.x == 0) {
+                __threadfence();
+                unsigned* ticket = &p.peers[p.rank]->ticket;
+                last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+                if (last) *ticket = 0u;  // every CTA has taken its ticket: ready for the next call
+            }
+            __syncthreads();
+            if (last) {
+                __threadfence();
+                allsum_epilogue(p);
+            }
+        }
     }
 }
 
-__global__ void fused_rows_combine(const double* partials, int n, double* out) {
-    if (blockIdx.x != 0 || threadIdx.x != 0) return;
-    double s = 0.0;
-    for (int i = 0; i < n; ++i) s = __dadd_rn(s, partials[i]);
-    *out = s;
+// Sum of the per-CTA partials (tree_sum_256: the loads overlap, the order is fixed).
+__global__ void __launch_bounds__(256) fused_rows_combine(const double* partials, int n, double* out) {
+    __shared__ double sm[8];
+    const double t = tree_sum_256(partials, n, sm);
+    if (threadIdx.x == 0) *out = t;
 }
 
 template <int OP1, int OP2, class T>
@@ -308,11 +417,41 @@ int fused_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb
     else launch_ops<double>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
     int launches = 1;
     if (d_sum) {
-        fused_rows_combine<<<1, 32, 0, st>>>(p.partials, static_cast<int>(grid), d_sum);
+        fused_rows_combine<<<1, 256, 0, st>>>(p.partials, static_cast<int>(grid), d_sum);
         ++launches;
     }
     count_launch(launches);
     return check_launch("fused rows");
+}
+
+// Cross-GPU form: the launch above with the per-CTA partials in this rank's workspace and the
+// last-CTA epilogue enabled (see the file comment). Every rank must make the same calls with the
+// same epochs, in the same order.
+int fused_rows_allsum(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                      const ctb_view* y, int row_op, const ctb_view* idx, PeerWorkspace* const* d_peers,
+                      int rank, int world, uint64_t epoch, const ctb_view* out_sum, double* d_parts,
+                      uint64_t timeout_ns, unsigned long long* timeouts, PeerWorkspace* my_ws, cudaStream_t st) {
+    FusedRowsArgs p{};
+    bool vec, stage;
+    size_t smem;
+    unsigned grid;
+    if (int rc = plan_fused(op1, op2, a, b, c, y, row_op, idx, p, vec, stage, smem, grid)) return rc;
+    if (grid > static_cast<unsigned>(kPeerMaxCtas)) grid = kPeerMaxCtas;
+    p.partials = my_ws->partials;
+    p.peers = d_peers;
+    p.rank = rank;
+    p.world = world;
+    p.epoch = epoch;
+    p.timeout_ns = timeout_ns;
+    p.out_sum = out_sum->data;
+    p.out_sum_dtype = out_sum->dtype;
+    p.out_parts = d_parts;
+    p.timeouts = timeouts;
+    // with no rows every CTA still runs the epilogue path (the grid is at least one CTA)
+    if (a->dtype == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
+    else launch_ops<double>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
+    count_launch();
+    return check_launch("fused rows (cross-GPU sum)");
 }
 
 }  // namespace ctb

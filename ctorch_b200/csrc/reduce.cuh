@@ -8,7 +8,8 @@
 //   red_outer       reduced dim strided, kept dim contiguous (column reductions): each warp walks
 //                   rows of a 32*V-column strip, warps combine through shared memory
 //   red_general_*   any other layout: per-element coordinate decode
-//   red_finalize    deterministic fixed-order combine of split partials (the second pass)
+//   red_finalize    deterministic fixed-order combine of split partials (the second pass);
+//                   red_finalize_cta for few outputs with many partials (a CTA-wide fixed tree)
 // Replaces ctorch's one-thread-per-output axis kernels and whole-tensor two-pass kernels
 // (src/ops/reduction_ops_cuda.cu:92-350).
 //
@@ -670,6 +671,27 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_cta(
     }
 }
 
+// Second pass for few outputs with many partials each (a whole-tensor sum split over every SM):
+// one CTA per output; thread t folds partials t, t + 256, ... in order, then a fixed-shape tree
+// (warp shuffles, then the warps' results) combines the threads. The shape depends only on the
+// split count, so results are run-to-run identical; the partial loads overlap instead of forming
+// one thread's chain of dependent loads.
+template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize_cta(RedArgs p) {
+    using S = typename R::State;
+    __shared__ S smem[kRedBlock / 32];
+    const S* part = static_cast<const S*>(p.scratch);
+    for (int64_t k = blockIdx.x; k < p.kept; k += gridDim.x) {
+        S st = R::init();
+        for (int s = threadIdx.x; s < p.split; s += blockDim.x) R::combine(st, part[k * p.split + s]);
+        st = block_reduce<R>(st, smem);
+        if (threadIdx.x == 0) {
+            int64_t in_off, o1, o2;
+            red_decode_kept(p, static_cast<uint64_t>(k), in_off, o1, o2);
+            R::write(p, st, o1, o2);
+        }
+    }
+}
+
 // Second pass: combine the `split` partials of each output in split order.
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize(RedArgs p) {
     using S = typename R::State;
@@ -731,7 +753,10 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
         break;
     }
     if (a.split > 1) {
-        red_finalize<R><<<grid_for((a.kept + kRedBlock - 1) / kRedBlock, 8), kRedBlock, 0, st>>>(a);
+        if (a.split >= 64 && a.kept <= static_cast<int64_t>(sm_count()) * 8)
+            red_finalize_cta<R><<<grid_for(a.kept, 8), kRedBlock, 0, st>>>(a);
+        else
+            red_finalize<R><<<grid_for((a.kept + kRedBlock - 1) / kRedBlock, 8), kRedBlock, 0, st>>>(a);
         ++launches;
     }
     count_launch(launches);

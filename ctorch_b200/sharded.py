@@ -195,3 +195,79 @@ def sharded_index_select(table: torch.Tensor, indices: torch.Tensor, total: int,
 
     sh = row_shard(total, rank, world)
     return (select or index_select)(table, 0, indices[sh.start:sh.stop])
+
+
+class PeerStep:
+    """The one-pass step of this rank with the whole-job sum exchanged inside the same launch
+    (ctb_chain_rows_allsum): Y = op2(op1(X, r), r) for this rank's rows, the per-row argmin, and
+    sum(Y) over all ranks, the same on every rank. The last CTA of each rank's launch stores the
+    rank's float64 partial into every rank's workspace over NVLink (CUDA IPC mappings set up here
+    once), waits for the others' and adds them in rank order, so a step is one kernel launch with
+    no collective call. Every rank must construct it (it exchanges the IPC handles through
+    `group`) and call it the same number of times; the ranks must be on different GPUs.
+    The sum equals ShardedSum's (same per-rank partial, same rank order) bit for bit."""
+
+    def __init__(self, device: torch.device, rank: int, world: int, group=None, out_dtype=torch.float32,
+                 timeout_ns: int = 0):
+        import ctypes
+
+        from . import _capi as C
+
+        self.C, self.rank, self.world, self.device = C, rank, world, device
+        self.timeout_ns = timeout_ns
+        with torch.cuda.device(device):
+            ws = ctypes.c_void_p()
+            handle = ctypes.create_string_buffer(64)
+            self._check(C.lib.ctb_peer_alloc(ctypes.byref(ws), handle))
+            self.ws = ws.value
+            handles = [bytes(handle.raw)]
+            if world > 1:
+                import torch.distributed as dist
+
+                handles = [None] * world
+                dist.all_gather_object(handles, bytes(handle.raw), group=group)
+            self._opened = []
+            ptrs = []
+            for r in range(world):
+                if r == rank:
+                    ptrs.append(self.ws)
+                    continue
+                p = ctypes.c_void_p()
+                self._check(C.lib.ctb_peer_open(handles[r], ctypes.byref(p)))
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            self.peer_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.out = torch.zeros((), dtype=out_dtype, device=device)
+        self.parts = torch.zeros(world, dtype=torch.float64, device=device)
+        self.epoch = 0
+
+    def _check(self, rc):
+        if rc != self.C.OK:
+            raise RuntimeError(self.C.last_error())
+
+    def __call__(self, x_local: torch.Tensor, r: torch.Tensor, y: Optional[torch.Tensor] = None,
+                 k: Optional[torch.Tensor] = None, op1: str = "sub", op2: str = "mul", row_op: str = "min"):
+        C = self.C
+        codes = {"add": C.ADD, "sub": C.SUB, "mul": C.MUL, "div": C.DIV}
+        if y is None:
+            y = torch.empty_like(x_local)
+        if k is None:
+            k = torch.empty(x_local.shape[0], dtype=torch.int64, device=x_local.device)
+        self.epoch += 1
+        self._check(C.lib.ctb_chain_rows_allsum(
+            codes[op1], codes[op2], C.view(x_local), C.view(r), C.view(r), C.view(y),
+            C.MIN if row_op == "min" else C.MAX, C.view(k), self.peer_ptrs.data_ptr(), self.ws,
+            self.rank, self.world, self.epoch, C.view(self.out), self.parts.data_ptr(), self.timeout_ns,
+            C.stream_handle(x_local.device)))
+        return y, self.out, k
+
+    def close(self):
+        """Unmaps the peers' workspaces and frees this rank's (after a device synchronize)."""
+        if self.ws is None:
+            return
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            for p in self._opened:
+                self.C.lib.ctb_peer_close(p)
+            self.C.lib.ctb_peer_free(self.ws)
+        self._opened, self.ws = [], None

@@ -215,6 +215,39 @@ CTB_API int ctb_chain_rows(int op1, int op2, const ctb_view* a, const ctb_view* 
                            const ctb_view* y, int row_op, const ctb_view* row_index, double* d_sum,
                            void* scratch, size_t scratch_bytes, ctb_stream stream);
 
+/* ---- the one-pass step across GPUs: compute and the sum's exchange in one launch ---- */
+
+/* Bytes of one rank's peer workspace (allocated by ctb_peer_alloc). */
+CTB_API size_t ctb_peer_workspace_bytes(void);
+
+/* Allocates this rank's peer workspace on the current device (zeroed) and writes its CUDA IPC
+ * handle (64 bytes) to ipc_handle for the other ranks of the node. */
+CTB_API int ctb_peer_alloc(void** d_workspace, void* ipc_handle);
+
+/* Maps another rank's workspace (from its IPC handle) into this process. */
+CTB_API int ctb_peer_open(const void* ipc_handle, void** d_peer_workspace);
+
+/* Unmaps a workspace opened with ctb_peer_open; frees this rank's own. */
+CTB_API int ctb_peer_close(void* d_peer_workspace);
+CTB_API int ctb_peer_free(void* d_workspace);
+
+/* ctb_chain_rows over this rank's rows, with the whole-tensor sum taken across `world` ranks in
+ * the same launch: the last CTA of the launch stores this rank's float64 partial over NVLink into
+ * slot `rank` of every rank's workspace (d_peer_workspaces: device array of the world workspace
+ * addresses, this rank's own at [rank]), waits until every rank's slot in its own workspace
+ * carries `epoch`, and writes out_sum (0-d float32/float64) = the rank partials added in rank
+ * order, the same on every rank, plus the partials to d_rank_partials [world] when not NULL.
+ * Every rank makes the same calls with epoch = 1, 2, 3, ... Each wait is bounded by timeout_ns
+ * (0: one second); a wait that runs out is counted (ctb_wait_timeouts) and out_sum is left
+ * unwritten. The ranks must run on different GPUs. No ctorch counterpart (ctorch has no
+ * multi-GPU layer); per rank it is ctb_chain_rows, and the sum is ctorch's whole-tensor sum
+ * (src/ops/reduction_ops_cpu.cpp:463) of the row-sharded y. */
+CTB_API int ctb_chain_rows_allsum(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                                  const ctb_view* y, int row_op, const ctb_view* row_index,
+                                  void* const* d_peer_workspaces, void* d_my_workspace, int rank, int world,
+                                  uint64_t epoch, const ctb_view* out_sum, double* d_rank_partials,
+                                  uint64_t timeout_ns, ctb_stream stream);
+
 /* ---- sharded reductions (multi-GPU layer) ---- */
 
 /* Scratch bytes for ctb_sum_partial. */

@@ -3,8 +3,12 @@
 - ctb_minmax_combine on one GPU, fed with the per-shard results of G emulated shards (each the
   backend's own max/min over its rows), against the oracle's reduction of the whole tensor:
   bit-exact, for every dtype, with NaNs and ties that straddle shard boundaries.
-- Two NCCL ranks on two GPUs (skipped with fewer): the sharded sum, the sharded column max/min
-  and the one-pass sharded step, each against the same computation on one GPU.
+- The one-launch step with the sum exchanged over NVLink (PeerStep / ctb_chain_rows_allsum): a
+  world of one against the unfused step, and a world of two with one rank missing, whose bounded
+  wait must run out and be counted.
+- Two NCCL ranks on two GPUs (skipped with fewer): the sharded sum, the sharded column max/min,
+  the one-pass sharded step and the one-launch step, each against the same computation on one GPU
+  or on the NCCL path.
 """
 import os
 import socket
@@ -89,6 +93,74 @@ def test_minmax_combine_rejects_bad_arguments(cuda_ok):
                                     C.stream_handle()) == C.ERR_DTYPE
 
 
+def test_peer_step_on_one_gpu_matches_the_unfused_step(cuda_ok):
+    """World of one: the single launch gives Y and k bit-identical to chain_rows and the same sum
+    bits as the partial -> combine path; repeated calls (epochs 1, 2, 3) stay consistent, which
+    also checks that the last CTA resets the completion ticket."""
+    import torch
+
+    import ctorch_b200 as cb
+    from ctorch_b200 import _capi as C
+    from ctorch_b200.sharded import PeerStep, ShardedSum, sharded_step_fused
+    from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
+
+    dev = torch.device("cuda", 0)
+    before = C.wait_timeouts()
+    x = device_fill(torch.empty(3001, 1024, device=dev), NORMAL, 11, 0, 0.0, 1.0)
+    r = device_fill(torch.empty(1, 1024, device=dev), UNIFORM, 11, 1, -1.0, 1.0)
+    y0, s0, k0 = sharded_step_fused(x, r, ShardedSum(dev, 1))
+    peer = PeerStep(dev, 0, 1)
+    try:
+        for _ in range(3):
+            y, s, k = peer(x, r)
+            assert torch.equal(y, y0) and torch.equal(k, k0)
+            assert s.item() == s0.item() and s.dtype == s0.dtype
+        empty = torch.empty(0, 1024, device=dev)
+        _, s_empty, _ = peer(empty, r)
+        assert s_empty.item() == 0.0
+    finally:
+        peer.close()
+    assert C.wait_timeouts() == before
+
+
+def test_peer_step_with_a_missing_rank_times_out(cuda_ok):
+    """A world of two with only one rank: the wait for rank 1's partial (a slot nothing writes)
+    gives up after its 5 ms limit, is counted, leaves the sum unwritten, and the device keeps
+    working."""
+    import ctypes
+
+    import torch
+
+    import ctorch_b200 as cb
+    from ctorch_b200 import _capi as C
+
+    dev = torch.device("cuda", 0)
+    ws, other = ctypes.c_void_p(), ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    assert C.lib.ctb_peer_alloc(ctypes.byref(ws), h) == C.OK, C.last_error()
+    assert C.lib.ctb_peer_alloc(ctypes.byref(other), h) == C.OK, C.last_error()
+    try:
+        peers = torch.tensor([ws.value, other.value], dtype=torch.int64, device=dev)
+        x = torch.randn(64, 256, device=dev)
+        r = torch.randn(1, 256, device=dev)
+        y = torch.empty_like(x)
+        k = torch.empty(64, dtype=torch.int64, device=dev)
+        out = torch.full((), -7.0, device=dev)
+        before = C.wait_timeouts()
+        rc = C.lib.ctb_chain_rows_allsum(C.SUB, C.MUL, C.view(x), C.view(r), C.view(r), C.view(y), C.MIN,
+                                         C.view(k), peers.data_ptr(), ws.value, 0, 2, 1, C.view(out), None,
+                                         5_000_000, C.stream_handle())
+        assert rc == C.OK, C.last_error()
+        torch.cuda.synchronize()
+        assert C.wait_timeouts() == before + 1
+        assert out.item() == -7.0
+        assert torch.equal(y, cb.binary_chain("sub", "mul", x, r, r))  # the step itself still ran
+    finally:
+        C.lib.ctb_peer_free(ws)
+        C.lib.ctb_peer_free(other)
+    assert cb.sum(torch.ones(5, device=dev)).item() == 5.0
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -102,7 +174,7 @@ def _nccl_worker(rank, world, port, results):
     import torch.distributed as dist
 
     import ctorch_b200 as cb
-    from ctorch_b200.sharded import ShardedColumnMinMax, ShardedSum, row_shard, sharded_step_fused
+    from ctorch_b200.sharded import PeerStep, ShardedColumnMinMax, ShardedSum, row_shard, sharded_step_fused
     from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -123,9 +195,19 @@ def _nccl_worker(rank, world, port, results):
         mv, mi = mx(local)
         mn = ShardedColumnMinMax("min", total, cols, torch.float32, dev, world)
         nv, ni = mn(local)
+        peer = PeerStep(dev, rank, world)
+        try:
+            for _ in range(3):
+                py, ps, pk = peer(local, r)
+            torch.cuda.synchronize()
+            peer_ok = torch.equal(py, y) and torch.equal(pk, k) and ps.item() == s.item()
+            peer_parts = peer.parts.cpu()
+        finally:
+            peer.close()
         torch.cuda.synchronize()
         out = {"s": float(s), "k": k.cpu(), "y_sum": float(y.double().sum()), "mv": mv.cpu(), "mi": mi.cpu(),
-               "nv": nv.cpu(), "ni": ni.cpu()}
+               "nv": nv.cpu(), "ni": ni.cpu(), "peer_ok": peer_ok, "peer_parts": peer_parts,
+               "timeouts": cb._capi.wait_timeouts()}
         if rank == 0:  # the whole tensor on one GPU
             y1 = cb.binary_chain("sub", "mul", full, r, r)
             out["ref"] = {"s": float(cb.sum(y1)), "k": cb.argmin(y1, 1).cpu(), "max": cb.max(full, 0, False),
@@ -159,3 +241,6 @@ def test_sharded_layer_on_two_gpus(cuda_ok):
         assert abs(o["s"] - ref["s"]) <= 1e-5 * max(1.0, abs(ref["s"]))
         assert torch.equal(o["mv"], ref["max"][0]) and torch.equal(o["mi"], ref["max"][1])
         assert torch.equal(o["nv"], ref["min"][0]) and torch.equal(o["ni"], ref["min"][1])
+        assert o["peer_ok"], f"rank {r}: the one-launch step differs from the NCCL step"
+        assert torch.equal(o["peer_parts"], results[0]["peer_parts"])
+        assert o["timeouts"] == 0
