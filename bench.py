@@ -5,12 +5,13 @@ Workload (the multi-GPU configuration of the hot path): X float32 [262144, 8192]
 (seed 4), rows split into contiguous blocks across the ranks, and r float32 [1, 8192] ~ U(-1, 1)
 (seed 4, stream 1) on every rank. One step:
     Y = (X - r) * r          bit-identical to ctorch's sub then mul
-    s = sum(Y)               float64 partial per rank, NCCL all-gather, rank-order combine
+    s = sum(Y)               float64 partial per rank, exchanged between ranks, rank-order sum
     k = argmin(Y, dim=1)     per row, first index on ties
-computed in one pass over each rank's rows (ctb_chain_rows: the chain with a row-argmin and
-float64-sum epilogue), then the 8-byte partials all-gathered. The same step as three kernels
-(chain, sum, argmin) and as ctorch's eager op sequence (sub, mul, sum, argmin) is timed too and
-reported beside it. Total work is fixed as GPUs are added (strong scaling). `value` is elements of X processed per
+computed by one kernel launch per rank (ctb_chain_rows_allsum): one pass over the rank's rows
+with a row-argmin and float64-sum epilogue, whose last CTA stores the rank's partial into every
+rank's workspace over NVLink, waits for the others' and adds them in rank order. The same step
+with the partials all-gathered through NCCL instead, as three kernels (chain, sum, argmin), and
+as ctorch's eager op sequence (sub, mul, sum, argmin) is timed too and reported beside it. Total work is fixed as GPUs are added (strong scaling). `value` is elements of X processed per
 second by the whole job, device-timed with CUDA events, max over ranks. Inputs (8 GiB in total)
 are larger than the 126 MB L2, so no flush is needed between steps.
 
@@ -201,7 +202,7 @@ def run_b200(args):
     import torch.distributed as dist
 
     import ctorch_b200 as cb
-    from ctorch_b200.sharded import ShardedSum, row_shard, sharded_step_fused
+    from ctorch_b200.sharded import PeerStep, ShardedSum, row_shard, sharded_step_fused
     from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
 
     rank, world, local = env_rank()
@@ -236,10 +237,14 @@ def run_b200(args):
     device_fill(x, NORMAL, SEED, 0, 0.0, 1.0, first=shard.start * COLS)
     device_fill(r, UNIFORM, SEED, 1, -1.0, 1.0)
     summer = ShardedSum(dev, world)
+    # the step: one launch per rank that also exchanges the sum's partials over NVLink
+    peer = PeerStep(dev, rank, world)
+    y_buf = torch.empty_like(x)
+    k_buf = torch.empty(shard.rows, dtype=torch.int64, device=dev)
     torch.cuda.synchronize()
 
     def step():
-        return sharded_step_fused(x, r, summer)
+        return peer(x, r, y_buf, k_buf)
 
     for _ in range(args.warmup):
         step()
@@ -247,7 +252,7 @@ def run_b200(args):
     barrier()
 
     K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler()
     if rank == 0:
@@ -259,11 +264,8 @@ def run_b200(args):
     start.record()
     for i in range(K):
         ev[i][0].record()
-        y, k, _ = cb.chain_rows("sub", "mul", x, r, r, row_op="min", out_sum=summer.partial)
+        step()
         ev[i][1].record()
-        summer.combine()
-        ev[i][2].record()
-        del y, k
     end.record()
     torch.cuda.synchronize()
     barrier()
@@ -271,10 +273,10 @@ def run_b200(args):
     clocks = sampler.stop() if rank == 0 else None
     elapsed = max_over_ranks(start.elapsed_time(end))
     fused_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in ev))
-    comb_ms = max_over_ranks(statistics.mean(e[1].elapsed_time(e[2]) for e in ev))
     total_launches = int(sum_over_ranks(launches))
 
     def time_steps(fn, n):
+        fn()  # warm-up (first-call allocations)
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -295,7 +297,11 @@ def run_b200(args):
         summer(y)
         cb.argmin(y, 1)
 
+    def nccl_step():
+        sharded_step_fused(x, r, summer)
+
     n_cmp = min(K, 20)
+    nccl_ms = time_steps(nccl_step, n_cmp)
     three_kernel_ms = time_steps(three_kernels, n_cmp)
     eager_ms = time_steps(eager_ops, n_cmp)
 
@@ -314,7 +320,7 @@ def run_b200(args):
         def e2e_step():
             xd.copy_(xh, non_blocking=True)
             rd.copy_(rh, non_blocking=True)
-            y, s, k = sharded_step_fused(xd, rd, summer)
+            y, s, k = peer(xd, rd, y_buf, k_buf)
             sh.copy_(s, non_blocking=True)
             kh.copy_(k, non_blocking=True)
 
@@ -333,8 +339,9 @@ def run_b200(args):
         e2e = {"value": ROWS * COLS / (e2e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": ROWS * COLS * 4 + world * COLS * 4,
                "d2h_bytes_per_step": ROWS * 8 + world * 4, "ms_per_step": e2e_ms,
-               "path": "pinned host X, r -> HBM; one-pass chain + row argmin + float64 partial "
-                       "(ctb_chain_rows), partials all-gathered and combined; s and k -> pinned host"}
+               "path": "pinned host X, r -> HBM; one launch per rank: chain + row argmin + float64 "
+                       "partial, partials exchanged over NVLink and combined (ctb_chain_rows_allsum); "
+                       "s and k -> pinned host"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -368,10 +375,12 @@ def run_b200(args):
             "gbs": (ROWS * COLS * 4 * 2 + ROWS * 8) / (ms_per_step / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "kernel": "fused_rows_kernel (ctb_chain_rows: (X - r) * r, row argmin, float64 sum)",
+                         "kernel": "fused_rows_kernel (ctb_chain_rows_allsum: (X - r) * r, row argmin, "
+                                   "float64 sum exchanged across ranks in the same launch)",
                          "algorithmic_bytes": fused_bytes,
                          "traffic": tpr * shard.rows if tpr else None},
-            "kernels_ms": {"chain_rows": fused_ms, "allgather_combine": comb_ms},
+            "kernels_ms": {"chain_rows_allsum": fused_ms},
+            "nccl_step_ms_per_step": nccl_ms,
             "three_kernel_ms_per_step": three_kernel_ms,
             "eager_ms_per_step": eager_ms,
             "gpu_launches": total_launches,
@@ -381,6 +390,7 @@ def run_b200(args):
         }
         print(json.dumps(line), flush=True)
     del summer
+    peer.close()
     if world > 1:
         barrier()
         dist.destroy_process_group()
