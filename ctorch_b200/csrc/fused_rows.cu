@@ -145,10 +145,30 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
         T* sc = sb + (p.c_is_b ? 0 : (C + kPad - 1) / kPad * kPad);
         const T b0 = p.b_bcast ? B[0] : T(0);
         const T c0 = p.c_bcast ? Cc[0] : T(0);
-        for (int j = threadIdx.x; j < C; j += blockDim.x) {
-            sb[j] = p.b_bcast ? b0 : B[j];
-            if (!p.c_is_b) sc[j] = p.c_bcast ? c0 : Cc[j];
-        }
+        // A row read as 16-byte packs, eight per thread in flight before any is stored, so the
+        // staging costs one round trip to L2 instead of one per element.
+        auto stage_row = [&](T* dst, const T* src, bool bcast, T v0) {
+            constexpr int PV = 16 / static_cast<int>(sizeof(T));
+            if (!bcast && V > 1) {  // V > 1: the rows are 16-byte aligned (pack path)
+                const int np = C / PV;
+                for (int j0 = threadIdx.x; j0 < np; j0 += 8 * blockDim.x) {
+                    Pack<T, PV> x[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (j0 + u * static_cast<int>(blockDim.x) < np)
+                            x[u] = load_pack<T, PV>(src + (j0 + u * static_cast<int>(blockDim.x)) * PV);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (j0 + u * static_cast<int>(blockDim.x) < np)
+                            *reinterpret_cast<Pack<T, PV>*>(dst + (j0 + u * static_cast<int>(blockDim.x)) * PV) = x[u];
+                }
+                for (int j = np * PV + threadIdx.x; j < C; j += blockDim.x) dst[j] = src[j];
+            } else {
+                for (int j = threadIdx.x; j < C; j += blockDim.x) dst[j] = bcast ? v0 : src[j];
+            }
+        };
+        stage_row(sb, B, p.b_bcast != 0, b0);
+        if (!p.c_is_b) stage_row(sc, Cc, p.c_bcast != 0, c0);
         __syncthreads();
         B = sb;
         Cc = sc;
