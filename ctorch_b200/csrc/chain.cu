@@ -6,9 +6,34 @@
 
 namespace ctb {
 
+// op2(op1(a, b), b): the chain when its third operand is the second one again, e.g. ctorch's
+// (X - r) * r. Read as two inputs, the broadcast row is loaded once per element instead of twice.
+template <int OP1, int OP2, class T> struct FnChainRepeat {
+    static constexpr bool kWideRows = OP1 != CTB_DIV && OP2 != CTB_DIV;
+    __device__ __forceinline__ T operator()(T a, T b) const {
+        return BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(a, b), b);
+    }
+};
+
+static bool same_view(const ctb_view* x, const ctb_view* y) {
+    if (x->data != y->data || x->dtype != y->dtype || x->ndim != y->ndim) return false;
+    for (int d = 0; d < x->ndim; ++d)
+        if (x->shape[d] != y->shape[d] || x->strides[d] != y->strides[d]) return false;
+    return true;
+}
+
 template <int OP1, int OP2, class T>
 int run_chain(const ctb_view* a, const ctb_view* b, const ctb_view* c, const ctb_view* out,
               cudaStream_t st) {
+    if (same_view(b, c)) {
+        using Fr = FnChainRepeat<OP1, OP2, T>;
+        constexpr int V2 = ew_vec<T, T, T, T, 2>();
+        const ctb_view* ins2[2] = {a, b};
+        const int sizes2[3] = {static_cast<int>(sizeof(T)), static_cast<int>(sizeof(T)), static_cast<int>(sizeof(T))};
+        EwPlan plan2;
+        if (int rc = plan_elementwise(out, ins2, 2, sizes2, V2, plan2)) return rc;
+        return launch_ew<Fr, T, T, T, T, 2>(plan2, Fr{}, st);
+    }
     using Fn = FnChain<OP1, OP2, T, T>;
     constexpr int V = ew_vec<T, T, T, T, 3>();
     const ctb_view* ins[3] = {a, b, c};

@@ -139,6 +139,15 @@ def test_chain_is_bitwise_the_eager_pair(cuda_ok, oracle, op1, op2, dt):
         assert_bitexact(got, ref, f"{op1}->{op2} {sx}", nan_payload=False)
         eager = getattr(cb, op2)(getattr(cb, op1)(tx, tr), tr).cpu().numpy()
         assert_bitexact(got, eager, "chain vs eager", nan_payload=False)
+        # a third operand of its own (the three-input kernel; the above reads r once per element)
+        c, tc = _pair(_rand(rng, sr, dt))
+        got3 = cb.binary_chain(op1, op2, tx, tr, tc).cpu().numpy()
+        ref3 = oracle.binary(op2, oracle.binary(op1, x, r), c)
+        assert_bitexact(got3, ref3, f"{op1}->{op2} {sx} distinct c", nan_payload=False)
+        # the same row through a different view is not the same operand, and must still agree
+        tr2 = tr.reshape(tr.shape)[..., :]
+        got_v = cb.binary_chain(op1, op2, tx, tr, tr2.expand(tr.shape) if tr.dim() == 2 else tr2).cpu().numpy()
+        assert_bitexact(got_v, ref, f"{op1}->{op2} {sx} aliased view", nan_payload=False)
 
 
 RED_LAYOUTS = {
