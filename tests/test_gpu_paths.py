@@ -47,6 +47,8 @@ BIN_LAYOUTS = {
     "rows_short_3d": ((50, 40, 8), [], (40, 1), []),
     "tiled": ((6, 200, 300), [], (6, 300, 200), [("permute", [0, 2, 1])]),
     "tiled_lhs": ((4, 130, 70), [("permute", [0, 2, 1])], (4, 70, 130), []),
+    "tiled_wide": ((3, 512, 384), [], (3, 384, 512), [("permute", [0, 2, 1])]),
+    "tiled_wide_edges": ((2, 300, 520), [("permute", [0, 2, 1])], (2, 520, 300), []),
     "general_offset": ((513, 257), [("slice", 0, 1, 513, 1)], (257,), []),
     "general_step": ((300, 200), [("slice", 1, 0, 200, 3)], (300, 1), []),
     "general_select": ((40, 7, 300), [("select", 1, 3)], (40, 300), [("slice", 1, 0, 300, 1)]),
