@@ -392,6 +392,7 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
     const int64_t sms = sm_count();
     plan.block = 256;
     plan.bulk = false;
+    plan.narrow = false;
     plan.bulk_fixup = false;
     a.split = 1;
     a.chunk = a.red;
@@ -433,6 +434,32 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
         break;
     }
     case RedPath::Outer: {
+        if (occ.cols_narrow > 0) {
+            // one CTA streams a contiguous block of whole rows; the rows are split over CTAs to fill
+            // the GPU, and the splits of each output are combined in order by red_finalize
+            plan.narrow = true;
+            plan.block = kNarrowBlock;
+            const int64_t vec = 16 / elem_bytes;
+            const int64_t np = a.N / vec;
+            const int64_t lanes = std::max<int64_t>(1, kNarrowBlock / np);
+            const int64_t tiles = a.kept / a.N;
+            const int64_t slots = sms * occ.cols_narrow;
+            int64_t split = 1;
+            const int64_t cap = std::max<int64_t>(1, (int64_t(4) << 20) / std::max<int64_t>(1, a.kept * state_bytes));
+            const int64_t max_split = std::max<int64_t>(1, std::min(a.K / (4 * lanes), cap));
+            if (tiles < 2 * slots) split = best_split(tiles, slots, max_split);
+            constexpr int64_t kMaxChunk = (int64_t(1) << 31) - 2;
+            split = std::max<int64_t>(split, (a.K + kMaxChunk - 1) / kMaxChunk);
+            int64_t chunk = (a.K + split - 1) / split;
+            split = (a.K + chunk - 1) / chunk;
+            a.split = static_cast<int>(split);
+            a.chunk = chunk;
+            a.aux2 = FastDiv(static_cast<uint64_t>(split));
+            const int64_t work = tiles * split;
+            plan.grid = static_cast<unsigned>(work < slots ? work : slots);
+            if (split > 1) scratch = static_cast<size_t>(a.kept * split) * state_bytes;
+            break;
+        }
         if (occ.cols_bulk > 0) {
             // Stream-K over (column tile, row): G CTAs take equal shares of the row-steps, so
             // every CTA streams the same number of bytes whatever the tile count; a tile shared

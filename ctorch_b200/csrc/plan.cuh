@@ -125,6 +125,7 @@ struct RedPlan {
     bool warp_rows = false;  // Inner: one warp per row instead of one CTA per row
     int col_tile = 0;        // Outer: columns per CTA
     bool bulk = false;       // Outer: bulk-copy column kernel (red_cols_bulk) instead of red_outer
+    bool narrow = false;     // Outer: contiguous narrow rows (red_cols_narrow) instead of red_outer
     bool bulk_fixup = false; // bulk: some column tile is shared by several CTAs (second pass)
     int64_t bulk_tiles = 0;  // bulk: column tiles
 };
@@ -141,7 +142,12 @@ int plan_reduction(const ctb_view* in, const ctb_view* out, const ctb_view* out2
 struct RedOcc {
     int inner_cta = 4, inner_warp = 4, outer = 4, general_cta = 4;
     int cols_bulk = 0;  // resident bulk column CTAs per SM; 0 when that kernel cannot take the plan
+    int cols_narrow = 0;  // resident narrow-column CTAs per SM; 0 when that kernel cannot take it
 };
+
+// Narrow column kernel: 256 threads, each owning one 16-byte column group of a contiguous
+// [K, N] block with N of at most 256 packs.
+constexpr int kNarrowBlock = 256;
 
 // Bulk column kernel geometry: each CTA has 4 consumer warps and 1 producer warp. A column tile
 // is 2 KiB of a row (128 threads x one 16-byte pack of columns each), a stage holds 8 rows of it.

@@ -630,6 +630,90 @@ template <class R> __global__ void __launch_bounds__(32 * kColsFixGroups) red_co
     }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Narrow column reductions (4- and 8-byte types): each batch row is a contiguous [K, N] block
+// whose rows are at most 1 KiB. A CTA streams whole rows [k0, k1) of one block as
+// a flat run of packs: thread t reads pack t, t + M, t + 2M, ... (M = np * lanes, a multiple of
+// the np packs of a row), so it always meets column group t % np, in rows t / np, t / np + lanes,
+// ... in increasing order, and every warp load is one contiguous 512-byte run. The `lanes`
+// threads of a column group are then combined in row order through shared memory; the CTA's
+// result is the output, or its split's partial (combined in split order by red_finalize).
+template <class R> __global__ void __launch_bounds__(kNarrowBlock) red_cols_narrow(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    constexpr int VE = 16 / static_cast<int>(sizeof(T));
+    constexpr int U = 4;  // packs in flight per thread
+    __shared__ S red[kNarrowBlock * VE];
+    const int np = static_cast<int>(p.N / VE);
+    const int lanes = kNarrowBlock / np > 0 ? kNarrowBlock / np : 1;
+    const int M = np * lanes;  // threads in use
+    const int t = threadIdx.x;
+    const bool active = t < M;
+    const int g = active ? t % np : 0, rl = active ? t / np : 0;
+    const int64_t batches = p.kept / p.N;
+    const int64_t total = batches * p.split;
+    for (int64_t w = blockIdx.x; w < total; w += gridDim.x) {
+        uint64_t b, sp;
+        p.aux2.divmod(static_cast<uint64_t>(w), b, sp);
+        int64_t in_off = 0, o1 = 0, o2 = 0;
+        {
+            uint64_t bb = b;
+            for (int d = p.rank_k - 2; d >= 0; --d) {
+                uint64_t q, c;
+                p.div_k[d].divmod(bb, q, c);
+                in_off += static_cast<int64_t>(c) * p.stride_k[d];
+                o1 += static_cast<int64_t>(c) * p.stride_o[d];
+                o2 += static_cast<int64_t>(c) * p.stride_o2[d];
+                bb = q;
+            }
+        }
+        const int64_t k0 = static_cast<int64_t>(sp) * p.chunk;
+        const int64_t k1 = k0 + p.chunk < p.K ? k0 + p.chunk : p.K;
+        typename R::Local st[VE];
+#pragma unroll
+        for (int e = 0; e < VE; ++e) st[e] = R::local_init();
+        if (active) {
+            const T* base = static_cast<const T*>(p.in) + in_off + g * VE;
+            for (int64_t k = k0 + rl; k < k1; k += static_cast<int64_t>(lanes) * U) {
+                Pack<T, VE> x[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t kk = k + static_cast<int64_t>(u) * lanes;
+                    if (kk < k1) x[u] = load_pack<T, VE>(base + kk * p.strideK);
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t kk = k + static_cast<int64_t>(u) * lanes;
+                    if (kk < k1) {
+                        const int32_t j = static_cast<int32_t>(kk - k0);
+#pragma unroll
+                        for (int e = 0; e < VE; ++e) R::fold_local(st[e], x[u].v[e], j);
+                    }
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < VE; ++e) red[t * VE + e] = R::widen(st[e], k0);
+        }
+        __syncthreads();
+        if (active && rl == 0) {
+            // thread g combines the lanes of column group g in row-lane order
+#pragma unroll
+            for (int e = 0; e < VE; ++e) {
+                S acc = red[g * VE + e];
+                for (int l = 1; l < lanes; ++l) R::combine(acc, red[(l * np + g) * VE + e]);
+                const int64_t col = static_cast<int64_t>(g) * VE + e;
+                if (p.split == 1) {
+                    R::write(p, acc, o1 + col, o2 + col);
+                } else {
+                    const int64_t kidx = static_cast<int64_t>(b) * p.N + col;
+                    static_cast<S*>(p.scratch)[kidx * p.split + static_cast<int64_t>(sp)] = acc;
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
 // One thread per output, folding the reduced subspace in row-major order (the CPU's order).
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_thread(RedArgs p) {
     using T = typename R::In;
@@ -732,6 +816,12 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
         break;
     case RedPath::Outer: {
         using T = typename R::In;
+        if constexpr (sizeof(T) >= 4) {
+            if (plan.narrow) {
+                red_cols_narrow<R><<<plan.grid, kNarrowBlock, 0, st>>>(a);
+                break;
+            }
+        }
         if (plan.bulk) {
             red_cols_bulk<R><<<plan.grid, kColsThreads, cols_smem_bytes(), st>>>(a);
             if (plan.bulk_fixup) {
@@ -790,6 +880,21 @@ inline bool cols_bulk_ok(const RedPlan& plan, int elem_bytes) {
     return a.K < (int64_t(1) << 31) - 1;
 }
 
+// Whether the narrow column kernel can take this Outer plan: each batch row is one contiguous
+// [K, N] block (rows back to back) of rows of at most 1 KiB, 16-byte aligned.
+inline bool cols_narrow_ok(const RedPlan& plan, int elem_bytes) {
+    const RedArgs& a = plan.args;
+    if (plan.path != RedPath::Outer) return false;
+    if (reinterpret_cast<uintptr_t>(a.in) % 16) return false;
+    if ((a.N * elem_bytes) % 16 || a.strideK != a.N) return false;
+    // rows up to 1 KiB (four or more threads a column group); wider rows stream better through
+    // the bulk kernel (argmax over 65536 x 1024 floats: 53 us bulk against 74 us here)
+    if (a.N * elem_bytes > 1024) return false;
+    for (int d = 0; d < a.rank_k - 1; ++d)
+        if ((a.stride_k[d] * elem_bytes) % 16) return false;
+    return a.K < (int64_t(1) << 31) - 1;
+}
+
 // Address of this device's timed-out-wait counter (async.cu); null if it cannot be had.
 unsigned long long* wait_timeout_counter();
 
@@ -823,7 +928,11 @@ int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint
     constexpr int V = outer_vec<T>();
     const bool vec_ok = outer_vec_ok(plan, sizeof(T), V);
     RedOcc occ;
-    if (cols_bulk_ok(plan, sizeof(T)) && cols_bulk_ready<R>()) {
+    if constexpr (sizeof(T) >= 4) {  // 1-byte columns: 16 chains a thread would not fit
+        if (cols_narrow_ok(plan, sizeof(T)))
+            occ.cols_narrow = resident_ctas(reinterpret_cast<const void*>(&red_cols_narrow<R>), kNarrowBlock);
+    }
+    if (occ.cols_narrow == 0 && cols_bulk_ok(plan, sizeof(T)) && cols_bulk_ready<R>()) {
         plan.args.timeouts = wait_timeout_counter();
         if (plan.args.timeouts)
             occ.cols_bulk = resident_ctas(reinterpret_cast<const void*>(&red_cols_bulk<R>), kColsThreads,

@@ -495,6 +495,12 @@ BULK_COLS = [
     ((7, 65, 304), 1),
     ((3000, 528), 0),
     ((2000, 1024), 0),
+    # contiguous rows narrower than 512 bytes (the narrow-column kernel for 4- and 8-byte types)
+    ((100_000, 64), 0),
+    ((50_001, 16), 0),
+    ((7, 300, 12), 1),
+    ((3, 1000, 32), 1),
+    ((4000, 100), 0),
 ]
 
 
