@@ -413,14 +413,21 @@ def run_case(args):
     rows = args.rows
     t = lambda shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
     case = args.case
-    if case in ("chain", "sum", "argmin", "sub", "chain_rows"):
+    if case in ("chain", "sum", "argmin", "sub", "chain_rows", "step"):
+        from ctorch_b200.sharded import PeerStep
+
         x = device_fill(t((rows, COLS)), NORMAL, SEED, 0, 0.0, 1.0)
         r = device_fill(t((1, COLS)), UNIFORM, SEED, 1, -1.0, 1.0)
         y = cb.binary_chain("sub", "mul", x, r, r)
         summer = ShardedSum(dev, 1)
-        fn = {"chain": lambda: cb.binary_chain("sub", "mul", x, r, r), "sub": lambda: cb.sub(x, r),
-              "sum": lambda: summer(y), "argmin": lambda: cb.argmin(y, 1),
-              "chain_rows": lambda: cb.chain_rows("sub", "mul", x, r, r, out_sum=summer.partial)}[case]
+        if case == "step":  # the bench's own step: one launch (world of one)
+            peer = PeerStep(dev, 0, 1)
+            k = torch.empty(rows, dtype=torch.int64, device=dev)
+            fn = lambda: peer(x, r, y, k)  # noqa: E731
+        else:
+            fn = {"chain": lambda: cb.binary_chain("sub", "mul", x, r, r), "sub": lambda: cb.sub(x, r),
+                  "sum": lambda: summer(y), "argmin": lambda: cb.argmin(y, 1),
+                  "chain_rows": lambda: cb.chain_rows("sub", "mul", x, r, r, out_sum=summer.partial)}[case]
     elif case in ("add", "relu"):
         a = device_fill(t((4096, 4096)), UNIFORM, 0, 0, -1.0, 1.0)
         b = device_fill(t((1, 4096)), UNIFORM, 0, 1, -1.0, 1.0)
