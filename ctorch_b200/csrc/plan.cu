@@ -393,6 +393,7 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
     plan.block = 256;
     plan.bulk = false;
     plan.narrow = false;
+    plan.row_group = 1;
     plan.bulk_fixup = false;
     a.split = 1;
     a.chunk = a.red;
@@ -405,10 +406,17 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
     case RedPath::Inner: {
         const int64_t K = a.K;
         if (K <= 65536 && a.kept >= sms * 16) {
-            // one warp per row, persistent grid of one wave
+            // one warp per row (or a group of 2 or 4 warps per long row when there are fewer than
+            // ~6 rows per resident warp), persistent grid of one wave
             plan.warp_rows = true;
-            const int64_t ctas = (a.kept + 7) / 8;
             const int64_t slots = sms * occ.inner_warp;
+            const int64_t warps = slots * 8;
+            plan.row_group = 1;
+            if (K * elem_bytes > 8192) {
+                while (plan.row_group < 4 && a.kept * plan.row_group < 6 * warps) plan.row_group *= 2;
+            }
+            const int64_t rows_per_cta = 8 / plan.row_group;
+            const int64_t ctas = (a.kept + rows_per_cta - 1) / rows_per_cta;
             plan.grid = static_cast<unsigned>(ctas < slots ? ctas : slots);
             break;
         }

@@ -123,6 +123,7 @@ struct RedPlan {
     int block = 256;
     unsigned grid = 1;
     bool warp_rows = false;  // Inner: one warp per row instead of one CTA per row
+    int row_group = 1;       // Inner warp rows: warps sharing one row (1, 2 or 4)
     int col_tile = 0;        // Outer: columns per CTA
     bool bulk = false;       // Outer: bulk-copy column kernel (red_cols_bulk) instead of red_outer
     bool narrow = false;     // Outer: contiguous narrow rows (red_cols_narrow) instead of red_outer

@@ -320,6 +320,38 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_warp(R
     }
 }
 
+// Rows shared by a group of G warps (G = 2 or 4) of one CTA, for long rows that are too few to
+// keep every warp busy one row each to the end (8192 rows of 32 KiB over ~4700 warps leave the
+// second round of rows 70% full). The G warps fold interleaved packs of the row, then the
+// group's warp results are combined in warp order through shared memory (double-buffered by row
+// parity, one named barrier per row for the group's warps only).
+template <class R, int G> __global__ void __launch_bounds__(kRedBlock) red_inner_group(RedArgs p) {
+    using T = typename R::In;
+    using S = typename R::State;
+    constexpr int kGroups = kRedBlock / (32 * G);
+    __shared__ S part[2][kGroups][G];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int gib = wib / G, wig = wib % G;
+    const int64_t ngroups = static_cast<int64_t>(gridDim.x) * kGroups;
+    int parity = 0;
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * kGroups + gib; row < p.kept; row += ngroups) {
+        int64_t in_off, o1, o2;
+        red_decode_kept(p, static_cast<uint64_t>(row), in_off, o1, o2);
+        S st = R::init();
+        fold_contig<R>(static_cast<const T*>(p.in) + in_off, 0, p.K, st, wig * 32 + lane, 32 * G);
+        st = warp_reduce<R>(st);
+        if (lane == 0) part[parity][gib][wig] = st;
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + gib), "r"(32 * G) : "memory");
+        if (wig == 0 && lane == 0) {
+            S acc = part[parity][gib][0];
+#pragma unroll
+            for (int w = 1; w < G; ++w) R::combine(acc, part[parity][gib][w]);
+            R::write(p, acc, o1, o2);
+        }
+        parity ^= 1;
+    }
+}
+
 // Column strips: kept inner dim N contiguous, reduced dim K with stride strideK, batch dims in
 // front. CTA = 8 warps; warp w folds rows k0+w, k0+w+8, ... of a 32*V-column strip.
 template <class R, int V> __global__ void __launch_bounds__(kOuterBlock) red_outer(RedArgs p) {
@@ -811,8 +843,13 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
     int launches = 1;
     switch (plan.path) {
     case RedPath::Inner:
-        if (plan.warp_rows) red_inner_warp<R><<<plan.grid, kRedBlock, 0, st>>>(a);
-        else red_inner_cta<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+        if (plan.warp_rows) {
+            if (plan.row_group == 4) red_inner_group<R, 4><<<plan.grid, kRedBlock, 0, st>>>(a);
+            else if (plan.row_group == 2) red_inner_group<R, 2><<<plan.grid, kRedBlock, 0, st>>>(a);
+            else red_inner_warp<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+        } else {
+            red_inner_cta<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+        }
         break;
     case RedPath::Outer: {
         using T = typename R::In;

@@ -157,6 +157,8 @@ RED_LAYOUTS = {
     "inner_cta": ((96, 20_000), [], [1], True),
     "inner_split": ((3, 1_000_003), [], [1], False),
     "inner_warp": ((5000, 100), [], [1], False),
+    "inner_warp_group": ((3000, 4100), [], [1], False),
+    "inner_warp_group_offset": ((2600, 3001), [("slice", 1, 1, 3001, 1)], [1], True),
     "inner_whole": ((2_000_003,), [], None, False),
     "inner_offset_rows": ((300, 999), [("slice", 1, 1, 999, 1)], [1], False),
     "outer": ((3000, 520), [], [0], False),
