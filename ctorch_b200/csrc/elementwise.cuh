@@ -503,13 +503,19 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled(EwArgs p, Fn fn) {
 // each thread 4 pack loads of each input and 4 pack stores. Edge tiles fall back to elements.
 // Requires (checked on the host, EwArgs::tiled_vec): pack-aligned bases and every stride other than
 // the unit ones a multiple of 4 elements; the row-major input has unit inner stride.
-template <class Fn, class O, class I0, class I1, int XOP>
-__global__ void __launch_bounds__(kEwBlock) ew_tiled4(EwArgs p, Fn fn) {
+// TL: the tile's extent along l (the output's and the row-major operand's unit-stride dim), 64 or
+// 128; the CTA has TL / 64 x 256 threads, each moving 4 packs of each operand per tile. With
+// TL = 128 the row-major operand and the output move in 512-byte runs instead of 256 (DRAM reads
+// of 256-byte runs spaced a row apart are ~10% slower) at the same bytes in flight per thread.
+template <class Fn, class O, class I0, class I1, int XOP, int TL = kTile>
+__global__ void __launch_bounds__(TL / kTile * kEwBlock) ew_tiled4(EwArgs p, Fn fn) {
     using X = std::conditional_t<XOP == 1, I0, I1>;
     using Y = std::conditional_t<XOP == 1, I1, I0>;
     constexpr int YOP = XOP == 1 ? 2 : 1;
-    constexpr int kPer = kTile * kTile / 4 / kEwBlock;  // packs per thread (4)
-    __shared__ X tile[kTile][kTile + 1];
+    constexpr int TP = kTile;
+    constexpr int NT = TL / kTile * kEwBlock;
+    constexpr int kPer = TL * TP / 4 / NT;  // packs per thread (4)
+    __shared__ X tile[TL][TP + 1];
     const int r = p.rank - 1;
     const int pd = p.pdim;
     const int64_t L = p.shape[r];
@@ -537,9 +543,9 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled4(EwArgs p, Fn fn) {
             offY += static_cast<int64_t>(c) * p.stride[YOP][d];
             batch = q;
         }
-        const int64_t l0 = static_cast<int64_t>(tl) * kTile;
-        const int64_t p0 = static_cast<int64_t>(tp) * kTile;
-        const bool full = p0 + kTile <= P && l0 + kTile <= L;
+        const int64_t l0 = static_cast<int64_t>(tl) * TL;
+        const int64_t p0 = static_cast<int64_t>(tp) * TP;
+        const bool full = p0 + TP <= P && l0 + TL <= L;
         if (full) {
             const X* xt = xin + offX + p0 + l0 * sXl;
             const Y* yt = yin + offY + p0 * sYp + l0;
@@ -548,28 +554,28 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled4(EwArgs p, Fn fn) {
             Pack<Y, 4> yr[kPer];
 #pragma unroll
             for (int j = 0; j < kPer; ++j) {
-                const int k = threadIdx.x + j * kEwBlock;
-                const int li = k >> 4, pg = k & 15;  // X: pack pg of row li (along p)
+                const int k = threadIdx.x + j * NT;
+                const int li = k / (TP / 4), pg = k % (TP / 4);  // X: pack pg of row li (along p)
                 xr[j] = load_pack<X, 4>(xt + 4 * pg + li * sXl);
             }
 #pragma unroll
             for (int j = 0; j < kPer; ++j) {
-                const int k = threadIdx.x + j * kEwBlock;
-                const int pi = k >> 4, lg = k & 15;  // Y: pack lg of row pi (along l)
+                const int k = threadIdx.x + j * NT;
+                const int pi = k / (TL / 4), lg = k % (TL / 4);  // Y: pack lg of row pi (along l)
                 yr[j] = load_pack<Y, 4>(yt + pi * sYp + 4 * lg);
             }
 #pragma unroll
             for (int j = 0; j < kPer; ++j) {
-                const int k = threadIdx.x + j * kEwBlock;
-                const int li = k >> 4, pg = k & 15;
+                const int k = threadIdx.x + j * NT;
+                const int li = k / (TP / 4), pg = k % (TP / 4);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) tile[li][4 * pg + e] = xr[j].v[e];
             }
             __syncthreads();
 #pragma unroll
             for (int j = 0; j < kPer; ++j) {
-                const int k = threadIdx.x + j * kEwBlock;
-                const int pi = k >> 4, lg = k & 15;
+                const int k = threadIdx.x + j * NT;
+                const int pi = k / (TL / 4), lg = k % (TL / 4);
                 Pack<O, 4> o;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -581,14 +587,14 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled4(EwArgs p, Fn fn) {
             }
             __syncthreads();
         } else {
-            for (int k = threadIdx.x; k < kTile * kTile; k += kEwBlock) {
-                const int li = k >> 6, pi = k & 63;
+            for (int k = threadIdx.x; k < TL * TP; k += NT) {
+                const int li = k / TP, pi = k % TP;
                 const int64_t pp = p0 + pi, ll = l0 + li;
                 if (pp < P && ll < L) tile[li][pi] = xin[offX + pp + ll * sXl];
             }
             __syncthreads();
-            for (int k = threadIdx.x; k < kTile * kTile; k += kEwBlock) {
-                const int pi = k >> 6, li = k & 63;
+            for (int k = threadIdx.x; k < TL * TP; k += NT) {
+                const int pi = k / TL, li = k % TL;
                 const int64_t pp = p0 + pi, ll = l0 + li;
                 if (pp < P && ll < L) {
                     const X x = tile[li][pi];
@@ -731,7 +737,28 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
             const int64_t L = a.shape[a.rank - 1];
             const int64_t P = a.shape[a.pdim];
             const int64_t total = (a.n / (L * P)) * static_cast<int64_t>(a.aux.d) * static_cast<int64_t>(a.aux2.d);
-            if (a.tiled_vec) {
+            // 128-wide tiles along l (512 threads) for 4-byte types (8-byte ones already move
+            // 512-byte runs with 64-wide tiles); tiles along l recounted for them
+            constexpr bool kWideL = sizeof(I0) == 4 && sizeof(I1) == 4 && sizeof(O) == 4;
+            bool wide_done = false;
+            if constexpr (kWideL) {
+              if (a.tiled_vec && L >= 2 * kTile) {
+                EwArgs aw = a;
+                aw.aux = FastDiv(static_cast<uint64_t>((L + 2 * kTile - 1) / (2 * kTile)));
+                const int64_t tw = (a.n / (L * P)) * static_cast<int64_t>(aw.aux.d) * static_cast<int64_t>(aw.aux2.d);
+                auto launch = [&](auto k) {
+                    const int64_t slots = static_cast<int64_t>(sm_count()) *
+                                          resident_ctas(reinterpret_cast<const void*>(k), 2 * kEwBlock);
+                    const int64_t g = tw < slots ? tw : slots;
+                    k<<<static_cast<unsigned>(g < 1 ? 1 : g), 2 * kEwBlock, 0, st>>>(aw, fn);
+                };
+                if (a.xop == 1) launch(&ew_tiled4<Fn, O, I0, I1, 1, 2 * kTile>);
+                else launch(&ew_tiled4<Fn, O, I0, I1, 2, 2 * kTile>);
+                wide_done = true;
+              }
+            }
+            if (wide_done) {
+            } else if (a.tiled_vec) {
                 if (a.xop == 1) {
                     auto k = &ew_tiled4<Fn, O, I0, I1, 1>;
                     k<<<wave_grid(k, total), kEwBlock, 0, st>>>(a, fn);
