@@ -179,6 +179,35 @@ template <class O, class A, class B> constexpr int vec_elems() {
     return 16 / m;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Programmatic dependent launch. A second pass started with launch_dependent() may be scheduled
+// while the kernel before it in the stream is still running: once every CTA of that kernel has
+// called allow_dependents() (or exited), the second pass's CTAs take SM room as it frees up and
+// block in dependent_wait() until the first kernel has completed and its writes are visible. The
+// launch and CTA start-up of the second pass then overlap the first pass's tail. A kernel started
+// the ordinary way treats both instructions as no-ops.
+
+__device__ __forceinline__ void allow_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void dependent_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <class... P, class... A>
+cudaError_t launch_dependent(void (*kernel)(P...), unsigned grid, unsigned block, size_t smem,
+                             cudaStream_t st, A... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<P>(args)...);
+}
+
 inline int ceil_div_int(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
 // Grid size for a grid-stride kernel: enough CTAs to fill every SM `per_sm` times, never more

@@ -282,6 +282,7 @@ template <class R> __device__ __forceinline__ void fold_contig(const typename R:
 // kernels
 
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_cta(RedArgs p) {
+    allow_dependents();  // a second pass may start its CTAs during this one
     using T = typename R::In;
     using S = typename R::State;
     __shared__ S smem[32];
@@ -305,6 +306,7 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_cta(Re
 }
 
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_warp(RedArgs p) {
+    allow_dependents();  // a second pass may start its CTAs during this one
     using T = typename R::In;
     using S = typename R::State;
     const int lane = threadIdx.x & 31;
@@ -326,6 +328,7 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_warp(R
 // group's warp results are combined in warp order through shared memory (double-buffered by row
 // parity, one named barrier per row for the group's warps only).
 template <class R, int G> __global__ void __launch_bounds__(kRedBlock) red_inner_group(RedArgs p) {
+    allow_dependents();  // a second pass may start its CTAs during this one
     using T = typename R::In;
     using S = typename R::State;
     constexpr int kGroups = kRedBlock / (32 * G);
@@ -355,6 +358,7 @@ template <class R, int G> __global__ void __launch_bounds__(kRedBlock) red_inner
 // Column strips: kept inner dim N contiguous, reduced dim K with stride strideK, batch dims in
 // front. CTA = 8 warps; warp w folds rows k0+w, k0+w+8, ... of a 32*V-column strip.
 template <class R, int V> __global__ void __launch_bounds__(kOuterBlock) red_outer(RedArgs p) {
+    allow_dependents();  // a second pass may start its CTAs during this one
     using T = typename R::In;
     using S = typename R::State;
     constexpr int W = kOuterBlock / 32;
@@ -486,6 +490,8 @@ __device__ __forceinline__ int64_t cols_start(const RedArgs& p, int64_t c) {
 }
 
 template <class R> __global__ void __launch_bounds__(kColsThreads, 1) red_cols_bulk(RedArgs p) {
+    // No allow_dependents() here: red_cols_finalize CTAs resident beside this kernel slowed its
+    // stream (measured); the finalize still launches as a dependent grid once these CTAs exit.
     using T = typename R::In;
     using S = typename R::State;
     constexpr int NS = kColsStages;
@@ -612,6 +618,7 @@ template <class R> __global__ void __launch_bounds__(kColsThreads, 1) red_cols_b
 // group order. The combine order is fixed by the plan, so results are run-to-run identical.
 constexpr int kColsFixGroups = 8;
 template <class R> __global__ void __launch_bounds__(32 * kColsFixGroups) red_cols_finalize(RedArgs p) {
+    dependent_wait();  // the first pass has completed and its partials are visible
     using T = typename R::In;
     using S = typename R::State;
     constexpr int TW = cols_tile<T>();
@@ -671,6 +678,7 @@ template <class R> __global__ void __launch_bounds__(32 * kColsFixGroups) red_co
 // threads of a column group are then combined in row order through shared memory; the CTA's
 // result is the output, or its split's partial (combined in split order by red_finalize).
 template <class R> __global__ void __launch_bounds__(kNarrowBlock) red_cols_narrow(RedArgs p) {
+    allow_dependents();  // a second pass may start its CTAs during this one
     using T = typename R::In;
     using S = typename R::State;
     constexpr int VE = 16 / static_cast<int>(sizeof(T));
@@ -748,6 +756,7 @@ template <class R> __global__ void __launch_bounds__(kNarrowBlock) red_cols_narr
 
 // One thread per output, folding the reduced subspace in row-major order (the CPU's order).
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_thread(RedArgs p) {
+    allow_dependents();  // a second pass may start its CTAs during this one
     using T = typename R::In;
     using S = typename R::State;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -764,6 +773,7 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_thre
 
 // CTAs share one output's reduced range (few outputs, long strided reductions).
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_cta(RedArgs p) {
+    allow_dependents();  // a second pass may start its CTAs during this one
     using T = typename R::In;
     using S = typename R::State;
     __shared__ S smem[32];
@@ -793,6 +803,7 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_cta(
 // split count, so results are run-to-run identical; the partial loads overlap instead of forming
 // one thread's chain of dependent loads.
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize_cta(RedArgs p) {
+    dependent_wait();  // the first pass has completed and its partials are visible
     using S = typename R::State;
     __shared__ S smem[kRedBlock / 32];
     const S* part = static_cast<const S*>(p.scratch);
@@ -810,6 +821,7 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize_cta
 
 // Second pass: combine the `split` partials of each output in split order.
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize(RedArgs p) {
+    dependent_wait();  // the first pass has completed and its partials are visible
     using S = typename R::State;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -861,8 +873,11 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
         }
         if (plan.bulk) {
             red_cols_bulk<R><<<plan.grid, kColsThreads, cols_smem_bytes(), st>>>(a);
+            if (int rc = check_launch("reduction")) return rc;
             if (plan.bulk_fixup) {
-                red_cols_finalize<R><<<grid_for((a.kept + 31) / 32, 8), 32 * kColsFixGroups, 0, st>>>(a);
+                const cudaError_t e = launch_dependent(red_cols_finalize<R>, grid_for((a.kept + 31) / 32, 8),
+                                                       32 * kColsFixGroups, 0, st, a);
+                if (e != cudaSuccess) return fail(CTB_ERR_CUDA, std::string("reduction: ") + cudaGetErrorString(e));
                 ++launches;
             }
             break;
@@ -880,10 +895,13 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
         break;
     }
     if (a.split > 1) {
-        if (a.split >= 64 && a.kept <= static_cast<int64_t>(sm_count()) * 8)
-            red_finalize_cta<R><<<grid_for(a.kept, 8), kRedBlock, 0, st>>>(a);
-        else
-            red_finalize<R><<<grid_for((a.kept + kRedBlock - 1) / kRedBlock, 8), kRedBlock, 0, st>>>(a);
+        if (int rc = check_launch("reduction")) return rc;
+        const cudaError_t e =
+            a.split >= 64 && a.kept <= static_cast<int64_t>(sm_count()) * 8
+                ? launch_dependent(red_finalize_cta<R>, grid_for(a.kept, 8), kRedBlock, 0, st, a)
+                : launch_dependent(red_finalize<R>, grid_for((a.kept + kRedBlock - 1) / kRedBlock, 8), kRedBlock,
+                                   0, st, a);
+        if (e != cudaSuccess) return fail(CTB_ERR_CUDA, std::string("reduction: ") + cudaGetErrorString(e));
         ++launches;
     }
     count_launch(launches);
