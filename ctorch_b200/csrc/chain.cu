@@ -69,8 +69,13 @@ int chain_typed(int op1, int op2, const ctb_view* a, const ctb_view* b, const ct
     return fail(CTB_ERR_ARGUMENT, "unknown binary op");
 }
 
+int fused_chain_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                     const ctb_view* out, cudaStream_t st);  // fused_rows.cu; -1 when it does not apply
+
 int chain_dispatch(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
                    const ctb_view* out, cudaStream_t st) {
+    const int rc = fused_chain_rows(op1, op2, a, b, c, out, st);
+    if (rc != -1) return rc;
     if (out->dtype == CTB_FLOAT32) return chain_typed<float>(op1, op2, a, b, c, out, st);
     return chain_typed<double>(op1, op2, a, b, c, out, st);
 }

@@ -131,7 +131,9 @@ template <class T> __device__ __forceinline__ T extreme_ident(bool is_max) {
 // STAGE: b and c are copied once per CTA into shared memory (a 0-d scalar is expanded to a row),
 // so the per-element reads of the broadcast row never hold registers across the latency of the
 // loads of a; without STAGE (rows too long for shared memory) they are read through L1.
-template <int OP1, int OP2, class T, int V, bool STAGE>
+// RED = false: the chain alone (y only; no row extreme, no sum), for ctb_binary_chain on
+// row-broadcast operands.
+template <int OP1, int OP2, class T, int V, bool STAGE, bool RED = true>
 __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
     constexpr int U = 4;
     extern __shared__ __align__(16) unsigned char fr_smem[];
@@ -208,11 +210,13 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
                         const T cc = p.c_is_b ? bb : (c_row ? xc.v[e] : Cc[0]);
                         const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(xa[u].v[e], bb), cc);
                         o.v[e] = yv;
-                        sum = __dadd_rn(sum, static_cast<double>(yv));
-                        const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
-                        if (repl) {
-                            best = yv;
-                            bidx = v * V + e;
+                        if constexpr (RED) {
+                            sum = __dadd_rn(sum, static_cast<double>(yv));
+                            const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
+                            if (repl) {
+                                best = yv;
+                                bidx = v * V + e;
+                            }
                         }
                     }
                     if (yr) store_pack<T, V>(yr + static_cast<int64_t>(v) * V, o);
@@ -225,14 +229,16 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
             const T cc = p.c_is_b ? bb : (c_row ? Cc[j] : Cc[0]);
             const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(ar[j], bb), cc);
             if (yr) yr[j] = yv;
-            sum = __dadd_rn(sum, static_cast<double>(yv));
-            const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
-            if (repl) {
-                best = yv;
-                bidx = j;
+            if constexpr (RED) {
+                sum = __dadd_rn(sum, static_cast<double>(yv));
+                const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
+                if (repl) {
+                    best = yv;
+                    bidx = j;
+                }
             }
         }
-        if (p.idx) {
+        if (RED && p.idx) {
             // Combine lanes: NaN first (lowest index), then the extreme value, then the lower
             // index. A lane that saw only +-inf (the min/max identity) keeps index -1 = "empty".
 #pragma unroll
@@ -257,7 +263,7 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
             if (lane == 0) p.idx[row * p.idx_stride] = bidx < 0 ? 0 : bidx;
         }
     }
-    if (p.partials) {
+    if (RED && p.partials) {
         __shared__ double sm[8];
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, m));
@@ -294,8 +300,9 @@ __global__ void __launch_bounds__(256) fused_rows_combine(const double* partials
 }
 
 template <int OP1, int OP2, class T>
-static const void* pick_kernel(bool vec, bool stage) {
+static const void* pick_kernel(bool vec, bool stage, bool red) {
     constexpr int V = 16 / sizeof(T);
+    if (!red) return reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, true, false>);
     if (stage)
         return vec ? reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, true>)
                    : reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, 1, true>);
@@ -303,10 +310,15 @@ static const void* pick_kernel(bool vec, bool stage) {
                : reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, 1, false>);
 }
 
+// red = false only with vec && stage (fused_chain_rows checks both before it launches).
 template <int OP1, int OP2, class T>
-static void launch_typed(bool vec, bool stage, unsigned grid, size_t smem, const FusedRowsArgs& p,
+static void launch_typed(bool vec, bool stage, bool red, unsigned grid, size_t smem, const FusedRowsArgs& p,
                          cudaStream_t st) {
     constexpr int V = 16 / sizeof(T);
+    if (!red) {
+        fused_rows_kernel<OP1, OP2, T, V, true, false><<<grid, 256, smem, st>>>(p);
+        return;
+    }
     if (stage) {
         if (vec) fused_rows_kernel<OP1, OP2, T, V, true><<<grid, 256, smem, st>>>(p);
         else fused_rows_kernel<OP1, OP2, T, 1, true><<<grid, 256, smem, st>>>(p);
@@ -317,12 +329,12 @@ static void launch_typed(bool vec, bool stage, unsigned grid, size_t smem, const
 }
 
 template <class T>
-static void launch_ops(int op1, int op2, bool vec, bool stage, unsigned grid, size_t smem,
+static void launch_ops(int op1, int op2, bool vec, bool stage, bool red, unsigned grid, size_t smem,
                        const FusedRowsArgs& p, cudaStream_t st, const void** fn_out) {
 #define CTB_FR(O1, O2)                                                            \
     if (op1 == O1 && op2 == O2) {                                                 \
-        if (fn_out) *fn_out = pick_kernel<O1, O2, T>(vec, stage);                 \
-        else launch_typed<O1, O2, T>(vec, stage, grid, smem, p, st);              \
+        if (fn_out) *fn_out = pick_kernel<O1, O2, T>(vec, stage, red);            \
+        else launch_typed<O1, O2, T>(vec, stage, red, grid, smem, p, st);         \
         return;                                                                   \
     }
     CTB_FR(CTB_SUB, CTB_MUL) CTB_FR(CTB_ADD, CTB_MUL) CTB_FR(CTB_MUL, CTB_ADD) CTB_FR(CTB_SUB, CTB_DIV)
@@ -338,7 +350,7 @@ constexpr size_t kMaxStageBytes = 96 * 1024;
 // Validation + planning shared by the scratch query and the launch. Returns the grid.
 static int plan_fused(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
                       const ctb_view* y, int row_op, const ctb_view* idx, FusedRowsArgs& p,
-                      bool& vec, bool& stage, size_t& smem, unsigned& grid) {
+                      bool& vec, bool& stage, size_t& smem, unsigned& grid, bool red = true) {
     if (op1 < CTB_ADD || op1 > CTB_DIV || op2 < CTB_ADD || op2 > CTB_DIV)
         return fail(CTB_ERR_ARGUMENT, "unknown binary op");
     if (row_op != CTB_MIN && row_op != CTB_MAX) return fail(CTB_ERR_ARGUMENT, "row_op must be CTB_MIN or CTB_MAX");
@@ -391,9 +403,10 @@ static int plan_fused(int op1, int op2, const ctb_view* a, const ctb_view* b, co
     smem = (p.c_is_b ? 1 : 2) * row_bytes;
     stage = smem <= kMaxStageBytes;
     if (!stage) smem = 0;
+    if (!red && !(vec && stage)) return -1;  // the chain-only kernel needs both
     const void* fn = nullptr;
-    if (dt == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, 0, smem, p, nullptr, &fn);
-    else launch_ops<double>(op1, op2, vec, stage, 0, smem, p, nullptr, &fn);
+    if (dt == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, red, 0, smem, p, nullptr, &fn);
+    else launch_ops<double>(op1, op2, vec, stage, red, 0, smem, p, nullptr, &fn);
     if (smem > 48 * 1024) {
         if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
             return check_launch("fused rows smem attribute");
@@ -433,8 +446,8 @@ int fused_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb
             return check_launch("fused rows");
         return CTB_OK;
     }
-    if (a->dtype == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
-    else launch_ops<double>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
+    if (a->dtype == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, true, grid, smem, p, st, nullptr);
+    else launch_ops<double>(op1, op2, vec, stage, true, grid, smem, p, st, nullptr);
     int launches = 1;
     if (d_sum) {
         fused_rows_combine<<<1, 256, 0, st>>>(p.partials, static_cast<int>(grid), d_sum);
@@ -468,10 +481,69 @@ int fused_rows_allsum(int op1, int op2, const ctb_view* a, const ctb_view* b, co
     p.out_parts = d_parts;
     p.timeouts = timeouts;
     // with no rows every CTA still runs the epilogue path (the grid is at least one CTA)
-    if (a->dtype == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
-    else launch_ops<double>(op1, op2, vec, stage, grid, smem, p, st, nullptr);
+    if (a->dtype == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, true, grid, smem, p, st, nullptr);
+    else launch_ops<double>(op1, op2, vec, stage, true, grid, smem, p, st, nullptr);
     count_launch();
     return check_launch("fused rows (cross-GPU sum)");
+}
+
+// ctb_binary_chain when the operands are rows of a [rows, cols] matrix and b, c are rows broadcast
+// over it (or scalars): the row kernel above without its reductions. One warp per row with b and c
+// in shared memory keeps more rows' loads in flight per SM than the elementwise row tiles, whose
+// per-thread broadcast-row packs take registers. Measured against those tiles on B200, it is
+// 1.5-7% faster on rows of 32 KiB or more (8192+ float32, 4096+ float64 columns) and 2-4% slower
+// on rows of 4-16 KiB, so it takes rows of at least kChainRowBytesMin bytes (up to the staging
+// limit), and at least kChainRowsMin of them, so that a one-wave grid of warps has rows to spare.
+// Returns -1 (nothing launched) when the layout does not fit; the caller then plans the chain as
+// any elementwise op.
+constexpr int64_t kChainRowsMin = 16384;
+constexpr int64_t kChainRowBytesMin = 32 * 1024;
+
+int fused_chain_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
+                     const ctb_view* out, cudaStream_t st) {
+    const int nd = out->ndim;
+    if (nd < 1 || a->ndim != nd || a->dtype != out->dtype || b->dtype != out->dtype || c->dtype != out->dtype)
+        return -1;
+    const int64_t C = out->shape[nd - 1];
+    int64_t n = 1;
+    for (int d = 0; d < nd; ++d) n *= out->shape[d];
+    if (C * static_cast<int64_t>(dtype_size(out->dtype)) < kChainRowBytesMin || n == 0) return -1;
+    const int64_t R = n / C;
+    if (R < kChainRowsMin) return -1;
+    // a and out: the same shape, both contiguous row-major
+    int64_t expect = 1;
+    for (int d = nd - 1; d >= 0; --d) {
+        if (a->shape[d] != out->shape[d]) return -1;
+        if (out->shape[d] != 1 && (out->strides[d] != expect || a->strides[d] != expect)) return -1;
+        expect *= out->shape[d];
+    }
+    // b, c: one element, or one unit-stride row of C broadcast over every other dim
+    auto row_like = [&](const ctb_view* v) {
+        if (v->ndim > nd) return false;
+        int64_t m = 1;
+        for (int d = 0; d < v->ndim; ++d) m *= v->shape[d];
+        if (m == 1) return true;
+        for (int d = 0; d < v->ndim - 1; ++d)
+            if (v->shape[d] != 1) return false;
+        return v->ndim >= 1 && v->shape[v->ndim - 1] == C && v->strides[v->ndim - 1] == 1;
+    };
+    if (!row_like(b) || !row_like(c)) return -1;
+    ctb_view a2 = *a, y2 = *out;
+    a2.ndim = y2.ndim = 2;
+    a2.shape[0] = y2.shape[0] = R;
+    a2.shape[1] = y2.shape[1] = C;
+    a2.strides[0] = y2.strides[0] = C;
+    a2.strides[1] = y2.strides[1] = 1;
+    FusedRowsArgs p{};
+    bool vec, stage;
+    size_t smem;
+    unsigned grid;
+    const int rc = plan_fused(op1, op2, &a2, b, c, &y2, CTB_MIN, nullptr, p, vec, stage, smem, grid, false);
+    if (rc) return rc;  // -1: unaligned, or rows too long to stage
+    if (out->dtype == CTB_FLOAT32) launch_ops<float>(op1, op2, true, true, false, grid, smem, p, st, nullptr);
+    else launch_ops<double>(op1, op2, true, true, false, grid, smem, p, st, nullptr);
+    count_launch();
+    return check_launch("chain rows");
 }
 
 }  // namespace ctb

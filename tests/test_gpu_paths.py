@@ -152,6 +152,67 @@ def test_chain_is_bitwise_the_eager_pair(cuda_ok, oracle, op1, op2, dt):
         assert_bitexact(got_v, ref, f"{op1}->{op2} {sx} aliased view", nan_payload=False)
 
 
+CHAIN_ROW_CASES = [
+    # (x shape, b shape, c shape; None: c is b), each last dim replaced by the columns of a
+    # 32 KiB row (8192 float32 or 4096 float64)
+    ((16384, 1), (1, 1), (1, 1)),        # c distinct
+    ((2, 8192, 1), (1,), (1,)),          # 3-D matrix, 1-D rows
+    ((16384, 1), (1, 1), "scalar"),      # c a one-element tensor
+    ((16400, 1), (1,), None),            # c is b (read once)
+]
+
+
+@pytest.mark.parametrize("case", range(4))
+@pytest.mark.parametrize("op1,op2", [("sub", "mul"), ("mul", "add"), ("add", "div"), ("div", "sub")])
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_chain_row_kernel(cuda_ok, oracle, case, op1, op2, dt):
+    """Chains on at least 16384 rows of 32 KiB or more with broadcast-row operands take the
+    warp-per-row kernel (rows staged in shared memory); results stay bit-identical to the oracle's
+    eager pair, with special values in both the matrix and the rows. Each op pair runs two of the
+    four layouts (the layout index is rotated by the op pair), to bound the test time."""
+    import ctorch_b200 as cb
+
+    pairs = [("sub", "mul"), ("mul", "add"), ("add", "div"), ("div", "sub")]
+    if (case + pairs.index((op1, op2))) % 2:
+        pytest.skip("layout covered by the neighbouring op pair")
+    cols = 32 * 1024 // np.dtype(dt).itemsize
+    sx, sb, sc = CHAIN_ROW_CASES[case]
+    sx = sx[:-1] + (cols,)
+    sb = sb[:-1] + (cols,)
+    rng = np.random.default_rng(11 + case)
+    x = _rand(rng, sx, dt)
+    flat = x.reshape(-1)
+    flat[:64] = np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-40, -1e30, 3.0] * 8, dtype=dt)
+    b = _rand(rng, sb, dt)
+    b.reshape(-1)[:6] = np.array([0.0, -0.0, np.inf, np.nan, 1e-39, -2.0], dtype=dt)
+    x_, tx = _pair(x)
+    b_, tb = _pair(b)
+    if sc is None:
+        c_, tc = b_, tb
+    else:
+        c_, tc = _pair(_rand(rng, (1, 1) if sc == "scalar" else sc[:-1] + (cols,), dt))
+    got = cb.binary_chain(op1, op2, tx, tb, tc).cpu().numpy()
+    ref = oracle.binary(op2, oracle.binary(op1, x_, b_), c_)
+    assert_bitexact(got, ref, f"{op1}->{op2} {sx}", nan_payload=False)
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_chain_row_kernel_unaligned_falls_back(cuda_ok, oracle, dt):
+    """A matrix whose rows are not 16-byte aligned takes the elementwise kernels, same results."""
+    import torch
+    import ctorch_b200 as cb
+
+    cols = 32 * 1024 // np.dtype(dt).itemsize
+    rng = np.random.default_rng(5)
+    x = _rand(rng, (16384, cols + 1), dt)
+    b = _rand(rng, (1, cols), dt)
+    tx = torch.from_numpy(x).cuda()[:, 1:]
+    tb = torch.from_numpy(b).cuda()
+    got = cb.binary_chain("sub", "mul", tx, tb, tb).cpu().numpy()
+    xs = np.ascontiguousarray(x[:, 1:])
+    assert_bitexact(got, oracle.binary("mul", oracle.binary("sub", xs, b), b), "unaligned rows", nan_payload=False)
+
+
 RED_LAYOUTS = {
     # name: (shape, recipe, dims, keepdim)
     "inner_cta": ((96, 20_000), [], [1], True),
