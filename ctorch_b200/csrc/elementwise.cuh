@@ -256,7 +256,7 @@ __device__ __forceinline__ void ew_row_segment(const EwArgs& p, const Fn& fn, co
                 Pack<O, V> o;
 #pragma unroll
                 for (int e = 0; e < V; ++e) o.v[e] = div_by_row<O>(cvt<O>(x0[u].v[e]), d);
-                store_pack<O, V>(out + c * V, o);
+                store_pack_split<O, V>(out + c * V, o);
             }
         }
     } else {
@@ -379,14 +379,15 @@ __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_short(EwArgs p, Fn fn)
                     const RowDivisor<O> d = row_divisor<O>(cvt<O>(s1[u]));
 #pragma unroll
                     for (int e = 0; e < V; ++e) o.v[e] = div_by_row<O>(cvt<O>(x0[u].v[e]), d);
+                    store_pack_split<O, V>(out + oo[u], o);
                 } else {
 #pragma unroll
                     for (int e = 0; e < V; ++e)
                         o.v[e] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, b0 ? s0[u] : x0[u].v[e],
                                                                   b1 ? s1[u] : x1[u].v[e],
                                                                   b2 ? s2[u] : x2[u].v[e]);
+                    store_pack<O, V>(out + oo[u], o);
                 }
-                store_pack<O, V>(out + oo[u], o);
             }
         }
     }

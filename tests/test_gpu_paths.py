@@ -152,6 +152,36 @@ def test_chain_is_bitwise_the_eager_pair(cuda_ok, oracle, op1, op2, dt):
         assert_bitexact(got_v, ref, f"{op1}->{op2} {sx} aliased view", nan_payload=False)
 
 
+@pytest.mark.parametrize("offset", [0, 2, 4, 6])
+@pytest.mark.parametrize("op", ["add", "mul", "div"])
+def test_wide_output_packs_at_any_alignment(cuda_ok, oracle, op, offset):
+    """float64 results of float32 operands move in 32-byte packs; a pack that starts on a 32-byte
+    boundary is stored in one piece, any other one as two 16-byte halves. Outputs at element
+    offsets 0 and 4 (32-byte aligned) and 2 and 6 (16-byte only), in place, for the flat, row and
+    per-row-scalar kernels, must all equal the oracle and leave the bytes around them alone."""
+    import torch
+    import ctorch_b200 as cb
+
+    rng = np.random.default_rng(31 + offset)
+    for shape, bshape in (((300_000,), (300_000,)), ((96, 8192), (1, 8192)), ((64, 512, 1024), (1, 512, 1))):
+        n = int(np.prod(shape))
+        big = rng.standard_normal(n + 8)
+        a = big[offset:offset + n].reshape(shape).copy()
+        b = _rand(rng, bshape, np.float32) + np.float32(2.0)
+        tbig = torch.from_numpy(big).cuda()
+        ta = tbig[offset:offset + n].view(shape)
+        getattr(cb, op + "_")(ta, torch.from_numpy(b).cuda())
+        got = tbig.cpu().numpy()
+        assert_bitexact(got[offset:offset + n].reshape(shape), oracle.binary(op, a, b), f"{op} {shape} +{offset}",
+                        nan_payload=False)
+        untouched = np.concatenate([big[:offset], big[offset + n:]])
+        assert np.array_equal(np.concatenate([got[:offset], got[offset + n:]]), untouched), "wrote outside"
+    # a widening cast into a fresh (aligned) output
+    x = _rand(rng, (1_000_003,), np.float32)
+    got = cb.cast(torch.from_numpy(x).cuda(), torch.float64).cpu().numpy()
+    assert_bitexact(got, x.astype(np.float64), "cast f32->f64")
+
+
 CHAIN_ROW_CASES = [
     # (x shape, b shape, c shape; None: c is b), each last dim replaced by the columns of a
     # 32 KiB row (8192 float32 or 4096 float64)
