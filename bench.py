@@ -56,11 +56,26 @@ def base_config(world):
 
 # ------------------------------------------------------------------------------- CPU (ctorch)
 
-def host_inputs(rows):
-    from ctorch_b200.synth import NORMAL, UNIFORM, host_fill
+def host_synth():
+    """ctorch_b200/synth.py loaded as a standalone module (numpy only), so that the CPU legs never
+    import the package, whose import loads the CUDA kernel library: the reference arm's process
+    maps ctorch's code (oracle/_ref) and nothing of this backend."""
+    import importlib.util
 
-    x = host_fill((rows, COLS), "float32", NORMAL, SEED, 0, 0.0, 1.0)
-    r = host_fill((1, COLS), "float32", UNIFORM, SEED, 1, -1.0, 1.0)
+    name = "_ctb_host_synth"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, "ctorch_b200", "synth.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def host_inputs(rows):
+    sy = host_synth()
+    x = sy.host_fill((rows, COLS), "float32", sy.NORMAL, SEED, 0, 0.0, 1.0)
+    r = sy.host_fill((1, COLS), "float32", sy.UNIFORM, SEED, 1, -1.0, 1.0)
     return x, r
 
 
@@ -74,28 +89,65 @@ def ctorch_cpu_step(ref, x, r):
     return s, k
 
 
-def time_ctorch_cpu(rows, steps, warmup):
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def time_ctorch_cpu(rows, steps, warmup, threads=1):
+    """ctorch's CPU front-doors on `rows` rows of the workload, the rows split into contiguous
+    blocks over `threads` host threads. Each thread runs the whole step (sub, mul, sum, argmin)
+    on its block: ctorch's CPU kernels are single-threaded (`#pragma omp simd` only, no threading
+    runtime), so a row split is the only way its code uses more than one core, and it is the same
+    split the GPU ranks use. The blocks' float32 sums are then added in block order (in double) and
+    the row argmins stay per block. ctypes releases the GIL inside each call, and ctorch's CPU pool
+    allocator keeps one cache per thread. Returns (elements per second, seconds per step)."""
+    from concurrent.futures import ThreadPoolExecutor
+
     from oracle.oracle import ref as get_ref
 
     ref = get_ref()
     xh, rh = host_inputs(rows)
-    x, r = ref.tensor(xh), ref.tensor(rh)
-    for _ in range(warmup):
-        ctorch_cpu_step(ref, x, r)
-    ts = []
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        ctorch_cpu_step(ref, x, r)
-        ts.append(time.perf_counter() - t0)
+    threads = max(1, min(int(threads), rows))
+    bounds = [(rows * t // threads, rows * (t + 1) // threads) for t in range(threads)]
+    xs = [ref.tensor(xh[a:b]) for a, b in bounds]
+    r = ref.tensor(rh)
+    del xh
+    pool = ThreadPoolExecutor(max_workers=threads) if threads > 1 else None
+
+    def step():
+        if pool is None:
+            ctorch_cpu_step(ref, xs[0], r)
+            return
+        parts = list(pool.map(lambda x: ctorch_cpu_step(ref, x, r), xs))
+        total = 0.0
+        for s_block, _ in parts:
+            total += float(s_block.numpy())
+        return total
+
+    try:
+        for _ in range(warmup):
+            step()
+        ts = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            step()
+            ts.append(time.perf_counter() - t0)
+    finally:
+        if pool is not None:
+            pool.shutdown()
     per_step = statistics.mean(ts)
     return rows * COLS / per_step, per_step
 
 
-def calibrate_rows(budget_s, n_steps, probe_rows=1024):
-    """Rows per CPU step so that n_steps fit in budget_s (powers of two, 512..65536)."""
-    _, t = time_ctorch_cpu(probe_rows, 1, 0)
+def calibrate_rows(budget_s, n_steps, threads, probe_rows=1024):
+    """Rows per CPU step (a power of two, 512..65536) so that n_steps on `threads` threads fit in
+    budget_s, from a one-thread probe."""
+    _, t = time_ctorch_cpu(probe_rows, 1, 0, 1)
     per_row = t / probe_rows
-    rows = max(512, min(65536, int(budget_s / max(1, n_steps) / per_row)))
+    rows = max(512, min(65536, int(budget_s / max(1, n_steps) / per_row * threads)))
     p = 512
     while p * 2 <= rows:
         p *= 2
@@ -106,16 +158,18 @@ def run_reference(args):
     rank, world, _ = env_rank()
     if rank != 0:
         return 0
-    rows = args.cpu_rows or calibrate_rows(150.0, args.steps + args.warmup)
-    value, per_step = time_ctorch_cpu(rows, args.steps, args.warmup)
+    threads = host_threads()
+    rows = args.cpu_rows or calibrate_rows(150.0, args.steps + args.warmup, threads)
+    value, per_step = time_ctorch_cpu(rows, args.steps, args.warmup, threads)
     sample = (f"{rows} of {ROWS} rows per step ({rows * COLS} elements), ctorch front-doors "
-              f"sub, mul, sum, argmin on CPU tensors, 1 thread (ctorch's CPU path is single-threaded)")
+              f"sub, mul, sum, argmin on CPU tensors, rows split in {threads} blocks over {threads} "
+              f"host threads (ctorch's CPU kernels are single-threaded each)")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": base_config(world), "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -195,6 +249,22 @@ def ncu_traffic_per_row():
 
 # ------------------------------------------------------------------------------- GPU arm
 
+PLUGIN_CHECK = os.path.join(ROOT, "ctorch_b200", "ctorch_plugin", "_build", "plugin_check")
+
+
+def plugin_bench(reps=50, timeout=600):
+    """The hot-path ops through ctorch's own API with this backend linked in (plugin_check
+    --bench): per op, dispatch::call into preallocated outputs, the public front-door (allocation
+    + Storage zero-fill + kernel) and the zero-fill alone. A list of dicts, or None when the
+    plugin was not built (no ctorch sources at build time)."""
+    if not os.path.exists(PLUGIN_CHECK):
+        return None
+    r = subprocess.run([PLUGIN_CHECK, "--bench", str(reps)], capture_output=True, text=True, timeout=timeout)
+    out = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
+    if r.returncode != 0:
+        out.append({"error": f"plugin_check --bench exited {r.returncode}", "stderr": r.stderr[-400:]})
+    return out
+
 def run_b200(args):
     import datetime
 
@@ -230,6 +300,15 @@ def run_b200(args):
         t = torch.tensor([v], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
+
+    def check_exchange():
+        """Every one-launch step so far completed its cross-GPU exchange, on every rank (a wait
+        that ran out leaves NaN as the sum and is recorded in the rank's workspace)."""
+        done, failed = peer.status()
+        bad = max_over_ranks(float(failed != 0 or done != peer.epoch))
+        if bad:
+            raise cb.CommTimeoutError(f"rank {rank}: a cross-GPU exchange timed out (status {done}, {failed}; "
+                                      f"{peer.epoch} calls)")
 
     shard = row_shard(ROWS, rank, world)
     x = torch.empty((shard.rows, COLS), dtype=torch.float32, device=dev)
@@ -271,6 +350,14 @@ def run_b200(args):
     barrier()
     launches = cb.launch_count()
     clocks = sampler.stop() if rank == 0 else None
+    check_exchange()
+    # where a step's time goes on each rank (kernel-side timestamps of the last timed calls)
+    step_trace = PeerStep.trace_summary(peer.trace(min(K, 64)))
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, step_trace)
+    else:
+        gathered = [step_trace]
     elapsed = max_over_ranks(start.elapsed_time(end))
     fused_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in ev))
     total_launches = int(sum_over_ranks(launches))
@@ -307,6 +394,7 @@ def run_b200(args):
 
     # end to end: pinned host input -> device, step, device -> pinned host results
     e2e = None
+    xd = rd = None
     if not args.no_e2e:
         xh = torch.empty((shard.rows, COLS), dtype=torch.float32, pin_memory=True)
         xh.copy_(x)
@@ -336,6 +424,7 @@ def run_b200(args):
         a1.record()
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(a0.elapsed_time(a1)) / e2e_steps
+        check_exchange()
         e2e = {"value": ROWS * COLS / (e2e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": ROWS * COLS * 4 + world * COLS * 4,
                "d2h_bytes_per_step": ROWS * 8 + world * 4, "ms_per_step": e2e_ms,
@@ -345,12 +434,26 @@ def run_b200(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
         rows = args.cpu_rows or 32768
-        v, per_step = time_ctorch_cpu(rows, 2, 1)
-        cpu = {"value": v, "unit": UNIT, "cores": 1, "kind": "reference",
+        v, per_step = time_ctorch_cpu(rows, 2, 1, threads)
+        v1, per_step1 = time_ctorch_cpu(min(rows, 4096), 2, 1, 1)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "reference",
                "sample": f"{rows} of {ROWS} rows ({rows * COLS} elements) through ctorch's CPU "
-                         f"front-doors sub, mul, sum, argmin; mean of 2 steps after 1 warm-up, "
-                         f"{per_step:.2f} s per step"}
+                         f"front-doors sub, mul, sum, argmin, rows split over {threads} host threads; "
+                         f"mean of 2 steps after 1 warm-up, {per_step:.3f} s per step",
+               "one_thread": {"value": v1, "unit": UNIT, "cores": 1,
+                              "sample": f"{min(rows, 4096)} rows on one thread, {per_step1:.3f} s per step"}}
+
+    per_op, plugin = None, None
+    if rank == 0 and world == 1 and not args.no_per_op:
+        xd = rd = None  # noqa: F841 (the e2e buffers: 8 GiB)
+        torch.cuda.empty_cache()
+        per_op = []
+        sub = argparse.Namespace(steps=min(K, 50), warmup=3, no_cpu_baseline=args.no_cpu_baseline)
+        run_suite(sub, sink=per_op)
+        torch.cuda.empty_cache()
+        plugin = plugin_bench(reps=min(K, 50))
 
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -380,6 +483,7 @@ def run_b200(args):
                          "algorithmic_bytes": fused_bytes,
                          "traffic": tpr * shard.rows if tpr else None},
             "kernels_ms": {"chain_rows_allsum": fused_ms},
+            "step_trace_by_rank": gathered,
             "nccl_step_ms_per_step": nccl_ms,
             "three_kernel_ms_per_step": three_kernel_ms,
             "eager_ms_per_step": eager_ms,
@@ -387,6 +491,8 @@ def run_b200(args):
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "per_op": per_op,
+            "plugin_ops": plugin,
         }
         print(json.dumps(line), flush=True)
     del summer
@@ -401,8 +507,9 @@ def run_b200(args):
 
 def run_case(args):
     """Launches one kernel of the hot path a few times on a reduced input, for an ncu capture
-    (e.g. `ncu --set full -k regex:ew_rows -c 3 python bench.py --case chain --rows 16384`).
-    Inputs stay larger than L2 at the default sizes. Prints nothing to time."""
+    (e.g. `ncu --set full --clock-control none -k regex:ew_rows -c 3 python bench.py --case chain
+    --rows 4096 --warmup 0 --steps 3`, after the same command has run without ncu). Inputs stay
+    larger than L2 at the default sizes. Prints nothing to time."""
     import torch
 
     import ctorch_b200 as cb
@@ -432,10 +539,20 @@ def run_case(args):
         a = device_fill(t((4096, 4096)), UNIFORM, 0, 0, -1.0, 1.0)
         b = device_fill(t((1, 4096)), UNIFORM, 0, 1, -1.0, 1.0)
         fn = (lambda: cb.add(a, b)) if case == "add" else (lambda: cb.relu(a))
-    elif case in ("sum_rows", "argmax_cols", "max_cols", "prod_rows"):
+    elif case in ("sum_rows", "argmax_cols", "max_cols", "prod_rows", "sum_cols"):
         x = device_fill(t((8192, 8192)), NORMAL, 1, 0, 0.0, 1.0)
         fn = {"sum_rows": lambda: cb.sum(x, [1], True), "prod_rows": lambda: cb.prod(x, [1]),
-              "argmax_cols": lambda: cb.argmax(x, 0), "max_cols": lambda: cb.max(x, 0)}[case]
+              "argmax_cols": lambda: cb.argmax(x, 0), "max_cols": lambda: cb.max(x, 0),
+              "sum_cols": lambda: cb.sum(x, [0])}[case]
+    elif case == "cols_narrow":  # 256-byte rows: the flat narrow column kernel
+        x = device_fill(t((1_000_000, 64)), NORMAL, 1, 0, 0.0, 1.0)
+        fn = lambda: cb.argmax(x, 0)  # noqa: E731
+    elif case == "cols_outer":  # rows of 8190 floats (not a whole number of 16-byte chunks): the register kernel
+        x = device_fill(t((8192, 8190)), NORMAL, 1, 0, 0.0, 1.0)
+        fn = lambda: cb.max(x, 0)  # noqa: E731
+    elif case == "argmin_rows":
+        y = device_fill(t((rows, COLS)), NORMAL, SEED, 0, 0.0, 1.0)
+        fn = lambda: cb.argmin(y, 1)  # noqa: E731
     elif case == "index_select":
         tab = device_fill(t((1_000_000, 256)), NORMAL, 2, 0, 0.0, 1.0)
         idx = device_fill(t((rows * 16,), torch.int64), UNIFORM, 2, 2, 0, 999_999)
@@ -456,8 +573,9 @@ def run_case(args):
 
 # ------------------------------------------------------------------------------- per-op suite
 
-def run_suite(args):
-    """Per-op device time and GB/s for every op of the five configurations, one JSON line per op.
+def run_suite(args, sink=None):
+    """Per-op device time and GB/s for every op of the five configurations, one JSON line per op
+    (appended to `sink` instead when it is a list: the default run's `per_op` key).
 
     Each op (or, for configuration 1, whose working set is about the size of L2, a round of the op
     on 4 separate copies of its inputs) is captured in a CUDA graph and replayed `--steps` times
@@ -528,7 +646,10 @@ def run_suite(args):
                            "speedup": (elems / ms) / (ce / cms)}
         if note:
             line["note"] = note
-        print(json.dumps(line), flush=True)
+        if sink is not None:
+            sink.append(line)
+        else:
+            print(json.dumps(line), flush=True)
 
     def rt(x):  # ctorch CPU tensor of a device tensor's values
         return ref.tensor(x.cpu().numpy()) if ref is not None else None
@@ -624,9 +745,13 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=0, help="rows per CPU step (0 = auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-per-op", action="store_true",
+                    help="skip the per-op table (every op of the five configurations) and the ctorch-API "
+                         "timings that the default one-GPU run adds to its line")
     ap.add_argument("--case", default=None,
-                    help="profiling mode: launch one kernel (chain_rows, chain, sub, sum, argmin, add, relu, sum_rows, "
-                         "prod_rows, argmax_cols, max_cols, index_select, mul_t, div_b) --warmup + --steps times")
+                    help="profiling mode: launch one kernel (chain_rows, chain, sub, sum, argmin, step, add, relu, "
+                         "sum_rows, prod_rows, argmax_cols, max_cols, sum_cols, cols_narrow, cols_outer, argmin_rows, "
+                         "index_select, mul_t, div_b) --warmup + --steps times")
     ap.add_argument("--rows", type=int, default=16384, help="rows of X for --case (default 16384: 512 MiB)")
     ap.add_argument("--suite", action="store_true",
                     help="per-op device time, GB/s and ctorch CPU time for every op of the five configurations")

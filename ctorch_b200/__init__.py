@@ -7,7 +7,7 @@ of that ABI:
   * this package — the same ops for torch CUDA tensors (ops.py mirrors ctorch's public API and
     error types), plus the row-sharded multi-GPU workload (sharded.py).
 """
-from .errors import AliasError, DeviceError, DTypeError, Error, ShapeError  # noqa: F401
+from .errors import AliasError, CommTimeoutError, DeviceError, DTypeError, Error, ShapeError  # noqa: F401
 from .ops import (  # noqa: F401
     ValuesIndices,
     abs,

@@ -83,6 +83,8 @@ def _load() -> ctypes.CDLL:
         "ctb_peer_open": (i32, [vp, ctypes.POINTER(vp)]),
         "ctb_peer_close": (i32, [vp]),
         "ctb_peer_free": (i32, [vp]),
+        "ctb_peer_status": (i32, [vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
+        "ctb_peer_trace": (i32, [vp, ctypes.POINTER(ctypes.c_uint64)]),
         "ctb_chain_rows_allsum": (i32, [i32, i32, P, P, P, P, i32, P, vp, vp, i32, i32, u64, P, vp, u64, vp]),
         "ctb_fill_random": (i32, [P, i32, u64, u64, i64, ctypes.c_double, ctypes.c_double, vp]),
         "ctb_debug_plan_elementwise": (i32, [P, ctypes.POINTER(P), i32, i32, ctypes.c_char_p, i32,
@@ -92,6 +94,7 @@ def _load() -> ctypes.CDLL:
                                            ctypes.POINTER(ctypes.c_int),
                                            ctypes.POINTER(ctypes.c_int)]),
         "ctb_debug_fastdiv": (u64, [u64, u64]),
+        "ctb_debug_noalloc_fits": (i32, [sz]),
         "ctb_wait_timeouts": (i32, [ctypes.POINTER(ctypes.c_uint64)]),
         "ctb_debug_wait_timeout": (i32, [u64, ctypes.POINTER(ctypes.c_int)]),
     }

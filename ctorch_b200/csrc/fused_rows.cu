@@ -15,8 +15,8 @@
 // over NVLink into slot `rank` of every rank's workspace (an IPC mapping of each peer's memory)
 // with the call's epoch, waits until every rank's slot in its own workspace carries that epoch,
 // and adds the slots in rank order: the whole-job sum, on every rank, from the one launch. The
-// waits are bounded in time; a wait that runs out is counted (ctb_wait_timeouts) and the sum is
-// left unwritten.
+// waits are bounded in time; a wait that runs out is counted (ctb_wait_timeouts), recorded in the
+// workspace (ctb_peer_status) and leaves NaN as the sum.
 #include <limits>
 
 #include "async_copy.cuh"
@@ -77,6 +77,9 @@ __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
 }
 
 // Cross-GPU epilogue, run by every thread of the last CTA of this rank's launch (256 threads).
+// Slots are double-buffered by epoch parity and a slot is accepted only when it carries exactly
+// this call's epoch (peer.cuh). A wait that runs out leaves NaN in out_sum (and in the missing
+// ranks' entries of out_parts), records the epoch in the workspace's failed_epoch and is counted.
 __device__ void allsum_epilogue(const FusedRowsArgs& p) {
     __shared__ double sm8[8];
     __shared__ double rank_sum[kPeerMaxRanks];
@@ -89,38 +92,47 @@ __device__ void allsum_epilogue(const FusedRowsArgs& p) {
     }
     __syncthreads();
     const int g = threadIdx.x;
+    const int par = static_cast<int>(p.epoch & 1u);
     if (g < p.world) {
         // publish: value, then (after a system-scope fence) the epoch that marks it valid
-        PeerSlot* dst = &p.peers[g]->slots[p.rank];
+        PeerSlot* dst = &p.peers[g]->slots[par][p.rank];
         *reinterpret_cast<volatile double*>(&dst->value) = mine_sh;
         __threadfence_system();
         st_release_sys(&dst->epoch, p.epoch);
     }
     if (g < p.world) {
-        // wait for rank g's value in this rank's own workspace
-        PeerSlot* src = &p.peers[p.rank]->slots[g];
-        bool ok = ld_acquire_sys(&src->epoch) >= p.epoch;
+        // wait for rank g's value of this epoch in this rank's own workspace
+        PeerSlot* src = &p.peers[p.rank]->slots[par][g];
+        bool ok = ld_acquire_sys(&src->epoch) == p.epoch;
         if (!ok) {
             const uint64_t t0 = global_ns();
-            while (!(ok = ld_acquire_sys(&src->epoch) >= p.epoch))
+            while (!(ok = ld_acquire_sys(&src->epoch) == p.epoch))
                 if (global_ns() - t0 > p.timeout_ns) break;
         }
         if (ok) rank_sum[g] = *reinterpret_cast<volatile const double*>(&src->value);
-        else atomicExch(&ok_all, 0);
+        else {
+            rank_sum[g] = __longlong_as_double(0x7ff8000000000000ll);
+            atomicExch(&ok_all, 0);
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        if (!ok_all) {
-            note_timeout(p.timeouts);
-            return;
-        }
+        PeerWorkspace* me = p.peers[p.rank];
         double s = 0.0;
         for (int r = 0; r < p.world; ++r) {  // rank order
             s = __dadd_rn(s, rank_sum[r]);
             if (p.out_parts) p.out_parts[r] = rank_sum[r];
         }
+        if (!ok_all) {
+            s = __longlong_as_double(0x7ff8000000000000ll);
+            me->failed_epoch = p.epoch;
+            note_timeout(p.timeouts);
+        } else {
+            me->done_epoch = p.epoch;
+        }
         if (p.out_sum_dtype == CTB_FLOAT32) *static_cast<float*>(p.out_sum) = static_cast<float>(s);
         else *static_cast<double*>(p.out_sum) = s;
+        me->trace[p.epoch % kPeerTraceSlots][kTraceExchanged] = global_ns();
     }
 }
 
@@ -175,6 +187,8 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
         B = sb;
         Cc = sc;
     }
+    if (RED && p.peers && blockIdx.x == 0 && threadIdx.x == 0)
+        p.peers[p.rank]->trace[p.epoch % kPeerTraceSlots][kTraceStart] = global_ns();
     const bool b_row = STAGE || !p.b_bcast;
     const bool c_row = STAGE || !p.c_bcast;
     const T* __restrict__ A = static_cast<const T*>(p.a);
@@ -279,9 +293,15 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
             __shared__ int last;
             if (threadIdx.x == 0) {
                 __threadfence();
-                unsigned* ticket = &p.peers[p.rank]->ticket;
-                last = atomicAdd(ticket, 1u) == gridDim.x - 1;
-                if (last) *ticket = 0u;  // every CTA has taken its ticket: ready for the next call
+                PeerWorkspace* me = p.peers[p.rank];
+                const unsigned tk = atomicAdd(&me->ticket, 1u);
+                last = tk == gridDim.x - 1;
+                uint64_t* tr = me->trace[p.epoch % kPeerTraceSlots];
+                if (tk == 0) tr[kTraceFirstDone] = global_ns();
+                if (last) {
+                    me->ticket = 0u;  // every CTA has taken its ticket: ready for the next call
+                    tr[kTraceLastDone] = global_ns();
+                }
             }
             __syncthreads();
             if (last) {

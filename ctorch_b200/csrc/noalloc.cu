@@ -8,10 +8,10 @@
 // g_reduce_scratch below instead.
 //
 // The array is a file-scope __device__ variable, so host code cannot use its name as a device
-// address. On the first call on each device (with that device current) the entry point looks up
-// the array's device address with cudaGetSymbolAddress and caches it; make that first call before
-// any stream capture. Every later call on the device reuses the same array.
-#include <mutex>
+// address. Every call that needs scratch looks up the array's address on the current device with
+// cudaGetSymbolAddress (cheap once the module is loaded; the first call on a device loads it, so
+// make that first call before any stream capture). Nothing is cached, so the address stays right
+// after a device reset or a new primary context.
 #include <string>
 
 #include "common.cuh"
@@ -31,34 +31,31 @@ constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 
 __device__ __align__(256) unsigned char g_reduce_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
-
-// Device address of g_reduce_scratch on the current device, looked up once per device.
+// Device address of g_reduce_scratch in the current device's context.
 int scratch_address(void** out) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("ctb_reduce_noalloc: cudaGetDevice");
-    if (dev < 0 || dev >= kMaxDevices)
-        return fail(CTB_ERR_ARGUMENT, "ctb_reduce_noalloc: device ordinal out of range");
-    std::lock_guard<std::mutex> lock(g_mu);
-    if (g_scratch_ptr[dev] == nullptr) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_reduce_scratch);
-        if (e != cudaSuccess || p == nullptr) {
-            cudaGetLastError();
-            return fail(CTB_ERR_CUDA, std::string("ctb_reduce_noalloc: cudaGetSymbolAddress failed: ") +
-                                          cudaGetErrorString(e));
-        }
-        g_scratch_ptr[dev] = p;
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_reduce_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        return fail(CTB_ERR_CUDA, std::string("ctb_reduce_noalloc: cudaGetSymbolAddress failed: ") +
+                                      cudaGetErrorString(e));
     }
-    *out = g_scratch_ptr[dev];
+    *out = p;
     return CTB_OK;
 }
 
 }  // namespace
 
 size_t reduce_noalloc_capacity() { return kNoAllocScratchBytes; }
+
+// The size check of ctb_reduce_noalloc: CTB_OK when `need` bytes fit the fixed array.
+int noalloc_fits(size_t need) {
+    if (need <= kNoAllocScratchBytes) return CTB_OK;
+    return fail(CTB_ERR_SCRATCH, "ctb_reduce_noalloc: this reduction needs " + std::to_string(need) +
+                                     " bytes of scratch, more than the fixed " +
+                                     std::to_string(kNoAllocScratchBytes) +
+                                     " bytes; use ctb_reduce with caller-provided scratch");
+}
 
 // Same validation and plan as ctb_reduce (the caller checks dtypes), then the launch with the
 // static array as scratch. Split reductions write every partial slot before reading it, so the
@@ -69,11 +66,7 @@ int reduce_noalloc(int op, const ctb_view* in, const ctb_view* out, uint32_t mas
     int rc = minmax ? minmax_dispatch(op, in, out, nullptr, mask, nullptr, 0, nullptr, &need)
                     : sum_like_dispatch(op, in, out, mask, nullptr, 0, nullptr, &need);
     if (rc) return rc;
-    if (need > kNoAllocScratchBytes)
-        return fail(CTB_ERR_SCRATCH, "ctb_reduce_noalloc: this reduction needs " + std::to_string(need) +
-                                         " bytes of scratch, more than the fixed " +
-                                         std::to_string(kNoAllocScratchBytes) +
-                                         " bytes; use ctb_reduce with caller-provided scratch");
+    if ((rc = noalloc_fits(need))) return rc;
     void* scratch = nullptr;
     if (need > 0) {
         rc = scratch_address(&scratch);
@@ -84,3 +77,5 @@ int reduce_noalloc(int op, const ctb_view* in, const ctb_view* out, uint32_t mas
 }
 
 }  // namespace ctb
+
+extern "C" CTB_API int ctb_debug_noalloc_fits(size_t need) { return ctb::noalloc_fits(need); }

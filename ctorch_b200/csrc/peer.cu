@@ -1,5 +1,6 @@
 // peer.cu — host side of the cross-GPU one-pass sum: the per-rank workspace (allocation, CUDA IPC
 // export and import). The launch itself is ctb_chain_rows_allsum (capi.cu, fused_rows.cu).
+#include <cstddef>
 #include <cstring>
 #include <string>
 
@@ -56,6 +57,25 @@ CTB_API int ctb_peer_open(const void* ipc_handle, void** d_peer_workspace) {
 CTB_API int ctb_peer_close(void* d_peer_workspace) {
     const cudaError_t e = cudaIpcCloseMemHandle(d_peer_workspace);
     return e == cudaSuccess ? CTB_OK : cuda_fail("ctb_peer_close", e);
+}
+
+CTB_API int ctb_peer_status(const void* d_my_workspace, uint64_t* done_epoch, uint64_t* failed_epoch) {
+    if (!d_my_workspace || !done_epoch || !failed_epoch) return fail(CTB_ERR_ARGUMENT, "ctb_peer_status: null argument");
+    uint64_t st[2];
+    const cudaError_t e = cudaMemcpy(st, static_cast<const char*>(d_my_workspace) + offsetof(PeerWorkspace, done_epoch),
+                                     sizeof(st), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail("ctb_peer_status", e);
+    static_assert(offsetof(PeerWorkspace, failed_epoch) == offsetof(PeerWorkspace, done_epoch) + 8, "layout");
+    *done_epoch = st[0];
+    *failed_epoch = st[1];
+    return CTB_OK;
+}
+
+CTB_API int ctb_peer_trace(const void* d_my_workspace, uint64_t* out) {
+    if (!d_my_workspace || !out) return fail(CTB_ERR_ARGUMENT, "ctb_peer_trace: null argument");
+    const cudaError_t e = cudaMemcpy(out, static_cast<const char*>(d_my_workspace) + offsetof(PeerWorkspace, trace),
+                                     sizeof(PeerWorkspace::trace), cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? CTB_OK : cuda_fail("ctb_peer_trace", e);
 }
 
 CTB_API int ctb_peer_free(void* d_workspace) {

@@ -2,6 +2,8 @@
 // (cuda_backend.cpp) and compares every result with ctorch's own CPU path on the same inputs.
 //   plugin_check --registry   every CUDA dispatch slot is filled (needs no GPU)
 //   plugin_check              the ops on cuda:0 vs CPU (bit-exact, float sums to 1e-5 relative)
+//   plugin_check --bench      device time of the hot-path ops through ctorch's API on cuda:0,
+//                             one JSON line per (op, path); see bench() below
 #include "ctorch/dispatch.h"
 #include "ctorch/errors.h"
 #include "ctorch/ops/elementwise.h"
@@ -12,10 +14,16 @@
 
 #include "b200_cast.h"
 #include "ops/cast_cpu.h"
+#include "ops/reduction.h"
 
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <string>
@@ -147,10 +155,130 @@ int registry() {
     return missing ? 1 : 0;
 }
 
+// ---- --bench: the hot-path ops through ctorch's own API on cuda:0 ----
+//
+// Three paths per op:
+//   dispatch    dispatch::call<Op>(Device::Kind::CUDA, ...) into preallocated outputs: ctorch's
+//               dispatcher, this backend's C++ shim and its kernels, the pattern of ctorch's own
+//               benchmark (tests/bench/add_bench.cpp:79-90);
+//   front_door  the public function (ctorch::add, ctorch::sum, ...): the same plus the output's
+//               allocation through ctorch's caching allocator and the zero-fill its Storage does
+//               on construction (src/storage.cpp:33-56);
+//   zero_fill   that zero-fill alone (cudaMemset of the output's bytes), i.e. what an opt-in
+//               uninitialised Storage would take off the front door.
+// `us` is the mean device time per call over `reps` calls back to back between CUDA events on the
+// legacy stream (the stream the backend launches on); `us_sync` is ctorch's own measure, the
+// median host time of one call between two cudaDeviceSynchronize (so it includes the launch
+// latency). Configuration 1's inputs are used as 4 copies in turn (536 MB > the 126 MB L2); the
+// others exceed L2 on their own.
+
+double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+template <class F> void time_path(const char* cfg, const char* op, const char* path, double bytes, int reps, F&& f) {
+    for (int i = 0; i < 3; ++i) f(i);
+    cudaDeviceSynchronize();
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, cudaStreamLegacy);
+    for (int i = 0; i < reps; ++i) f(i);
+    cudaEventRecord(e1, cudaStreamLegacy);
+    cudaEventSynchronize(e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    std::vector<double> ts;
+    for (int i = 0; i < std::min(reps, 25); ++i) {
+        cudaDeviceSynchronize();
+        const double t0 = now_s();
+        f(i);
+        cudaDeviceSynchronize();
+        ts.push_back(now_s() - t0);
+    }
+    std::sort(ts.begin(), ts.end());
+    const double us = ms * 1e3 / reps;
+    const cudaError_t err = cudaGetLastError();
+    std::printf("{\"config\": \"%s\", \"op\": \"%s\", \"path\": \"%s\", \"us\": %.3f, \"us_sync\": %.3f, "
+                "\"gbs\": %.1f, \"algorithmic_bytes\": %.0f, \"reps\": %d, \"cuda\": \"%s\"}\n",
+                cfg, op, path, us, ts[ts.size() / 2] * 1e6, bytes / (us * 1e-6) / 1e9, bytes, reps,
+                cudaGetErrorString(err));
+    std::fflush(stdout);
+}
+
+int bench(int reps) {
+    const Device gpu = Device::cuda(0);
+    const auto K = Device::Kind::CUDA;
+    {  // configuration 1: add [4096,4096] + [1,4096], relu
+        const int64_t n = 4096;
+        std::vector<Tensor> A, B, C, O;
+        for (int c = 0; c < 4; ++c) {
+            A.push_back(make({n, n}, dtype::float32).to(gpu));
+            B.push_back(make({1, n}, dtype::float32).to(gpu));
+            C.push_back(add(A.back(), B.back()));
+            O.push_back(Tensor({n, n}, dtype::float32, gpu));
+        }
+        const double add_b = 2.0 * n * n * 4 + n * 4, relu_b = 2.0 * n * n * 4;
+        time_path("1", "add", "dispatch", add_b, reps, [&](int i) { dispatch::call<op::AddOp>(K, A[i & 3], B[i & 3], O[i & 3]); });
+        time_path("1", "add", "front_door", add_b, reps, [&](int i) { (void)add(A[i & 3], B[i & 3]); });
+        time_path("1", "relu", "dispatch", relu_b, reps, [&](int i) { dispatch::call<op::ReluOp>(K, C[i & 3], O[i & 3]); });
+        time_path("1", "relu", "front_door", relu_b, reps, [&](int i) { (void)relu(C[i & 3]); });
+        time_path("1", "[4096,4096] float32 output", "zero_fill", n * n * 4.0, reps,
+                  [&](int i) { cudaMemset(O[i & 3].storage().data(), 0, n * n * 4); });
+    }
+    {  // configuration 2: X [8192,8192]: sum/mean over dim 1 (keepdim), max/argmax over dim 0, prod dim 1
+        const int64_t n = 8192;
+        Tensor X = make({n, n}, dtype::float32).to(gpu);
+        Tensor s1({n, 1}, dtype::float32, gpu), v0({n}, dtype::float32, gpu), i0({n}, dtype::int64, gpu);
+        const ops::ReductionAxes ax1 = ops::canonicalise(X, {1});
+        const std::vector<int64_t> d1{1};
+        const double rd = double(n) * n * 4;
+        time_path("2", "sum dim=1 keepdim", "dispatch", rd + n * 4, reps, [&](int) { dispatch::call<op::SumOp>(K, X, s1, ax1); });
+        time_path("2", "sum dim=1 keepdim", "front_door", rd + n * 4, reps, [&](int) { (void)sum(X, d1, true); });
+        time_path("2", "mean dim=1 keepdim", "dispatch", rd + n * 4, reps, [&](int) { dispatch::call<op::MeanOp>(K, X, s1, ax1); });
+        time_path("2", "max dim=0 (values+indices)", "dispatch", rd + n * 12, reps,
+                  [&](int) { dispatch::call<op::MaxValIdxOp>(K, X, v0, i0, 0); });
+        time_path("2", "max dim=0 (values+indices)", "front_door", rd + n * 12, reps, [&](int) { (void)ctorch::max(X, int64_t{0}, false); });
+        time_path("2", "argmax dim=0", "dispatch", rd + n * 8, reps, [&](int) { dispatch::call<op::ArgmaxOp>(K, X, i0, 0); });
+        time_path("2", "argmax dim=0", "front_door", rd + n * 8, reps, [&](int) { (void)argmax(X, 0); });
+    }
+    {  // configuration 4: int32 [64,512,1024] * transpose(1,2) of float32 [64,1024,512]; / float64 [1,512,1]
+        Tensor I = make({64, 512, 1024}, dtype::int32).to(gpu);
+        Tensor F = make({64, 1024, 512}, dtype::float32).to(gpu);
+        Tensor D = make({1, 512, 1}, dtype::float64).to(gpu);
+        Tensor Ft = F.permute({0, 2, 1});
+        Tensor P({64, 512, 1024}, dtype::float32, gpu), Q({64, 512, 1024}, dtype::float64, gpu);
+        const double e = 64.0 * 512 * 1024;
+        // mixed operand dtypes reach the backend only through dispatch::call: ctorch's front-door
+        // casts first, on the host (src/ops/binary_ops_cpu.cpp:154-184)
+        time_path("4", "mul int32 x float32^T -> float32", "dispatch", e * 12, reps,
+                  [&](int) { dispatch::call<op::MulOp>(K, I, Ft, P); });
+        time_path("4", "div float32 / float64[1,512,1] -> float64", "dispatch", e * 12 + 4096, reps,
+                  [&](int) { dispatch::call<op::DivOp>(K, P, D, Q); });
+    }
+    {  // configuration 3: index_select of 4194304 rows from a float32 [1000000, 256] table
+        Tensor T = make({1000000, 256}, dtype::float32).to(gpu);
+        Tensor idx({4194304}, dtype::int64, Device::cpu());
+        auto* ip = static_cast<int64_t*>(idx.storage().data());
+        for (int64_t i = 0; i < 4194304; ++i) ip[i] = static_cast<int64_t>(next_u64() % 1000000);
+        Tensor ig = idx.to(gpu), out({4194304, 256}, dtype::float32, gpu);
+        const double b = 4194304.0 * 8 + 2.0 * 4194304 * 256 * 4;
+        const int r3 = std::max(3, reps / 10);
+        time_path("3", "index_select float32", "dispatch", b, r3, [&](int) { dispatch::call<op::IndexSelectOp>(K, T, 0, ig, out); });
+        time_path("3", "index_select float32", "front_door", b, r3, [&](int) { (void)index_select(T, 0, ig); });
+        time_path("3", "[4194304,256] float32 output", "zero_fill", 4194304.0 * 256 * 4, r3,
+                  [&](int) { cudaMemset(out.storage().data(), 0, size_t(4194304) * 256 * 4); });
+    }
+    return cudaDeviceSynchronize() == cudaSuccess ? 0 : 1;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
     if (argc > 1 && std::strcmp(argv[1], "--registry") == 0) return registry();
+    if (argc > 1 && std::strcmp(argv[1], "--bench") == 0) return bench(argc > 2 ? std::atoi(argv[2]) : 50);
     const Device gpu = Device::cuda(0);
 
     // elementwise, broadcast and views

@@ -19,3 +19,8 @@ class DeviceError(Error):
 
 class AliasError(Error):
     """In-place destination aliases a non-trivial view of an input (ctorch::AliasError)."""
+
+
+class CommTimeoutError(DeviceError):
+    """A rank of a cross-GPU exchange did not arrive within the wait's time limit (the C ABI's
+    bounded waits; no ctorch counterpart, ctorch has no multi-GPU layer)."""

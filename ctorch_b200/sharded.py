@@ -204,8 +204,12 @@ class PeerStep:
     rank's float64 partial into every rank's workspace over NVLink (CUDA IPC mappings set up here
     once), waits for the others' and adds them in rank order, so a step is one kernel launch with
     no collective call. Every rank must construct it (it exchanges the IPC handles through
-    `group`) and call it the same number of times; the ranks must be on different GPUs.
-    The sum equals ShardedSum's (same per-rank partial, same rank order) bit for bit."""
+    `group`) and call it the same number of times, on one stream; the ranks must be on different
+    GPUs. The sum equals ShardedSum's (same per-rank partial, same rank order) bit for bit.
+
+    A rank that does not arrive within `timeout_ns` (0: one second) makes the others' waits run
+    out: their sum of that call is NaN and the call is recorded in the workspace. The calls do not
+    synchronise the host; `check()` does, and raises CommTimeoutError if any call so far failed."""
 
     def __init__(self, device: torch.device, rank: int, world: int, group=None, out_dtype=torch.float32,
                  timeout_ns: int = 0):
@@ -260,6 +264,59 @@ class PeerStep:
             self.rank, self.world, self.epoch, C.view(self.out), self.parts.data_ptr(), self.timeout_ns,
             C.stream_handle(x_local.device)))
         return y, self.out, k
+
+    def status(self):
+        """(done_epoch, failed_epoch) of this rank's workspace: the last call whose exchange
+        completed and the last whose wait ran out (0: none). Synchronises the device."""
+        import ctypes
+
+        done, failed = ctypes.c_uint64(0), ctypes.c_uint64(0)
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            self._check(self.C.lib.ctb_peer_status(self.ws, ctypes.byref(done), ctypes.byref(failed)))
+        return done.value, failed.value
+
+    def trace(self, calls: Optional[int] = None):
+        """Per-call timestamps of this rank's last `calls` calls (at most 64; default all made,
+        capped at 64), oldest first, in ns of this GPU's %globaltimer: rows of (CTA 0 started,
+        first CTA done, last CTA done, exchange completed). Synchronises the device."""
+        import ctypes
+
+        import numpy as np
+
+        buf = (ctypes.c_uint64 * (64 * 4))()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            self._check(self.C.lib.ctb_peer_trace(self.ws, buf))
+        ring = np.frombuffer(buf, dtype=np.uint64).reshape(64, 4).astype(np.int64)
+        n = min(64, self.epoch if calls is None else calls, self.epoch)
+        epochs = range(self.epoch - n + 1, self.epoch + 1)
+        return np.stack([ring[e % 64] for e in epochs]) if n else np.zeros((0, 4), np.int64)
+
+    @staticmethod
+    def trace_summary(tr) -> dict:
+        """Medians (µs) over calls of a trace(): `rows` (CTA 0 start to the last CTA done),
+        `tail` (first to last CTA done: the one-wave grid's ragged end), `exchange` (last CTA
+        done to the exchange completed: NVLink latency plus the wait for slower ranks), `gap`
+        (previous call's exchange completed to this call's CTA 0 start: launch gap)."""
+        import numpy as np
+
+        if len(tr) == 0:
+            return {}
+        med = lambda a: float(np.median(a)) / 1e3 if len(a) else None  # noqa: E731
+        return {"rows_us": med(tr[:, 2] - tr[:, 0]), "tail_us": med(tr[:, 2] - tr[:, 1]),
+                "exchange_us": med(tr[:, 3] - tr[:, 2]), "gap_us": med(tr[1:, 0] - tr[:-1, 3]),
+                "calls": int(len(tr))}
+
+    def check(self):
+        """Raises CommTimeoutError unless every call so far completed its exchange."""
+        from .errors import CommTimeoutError
+
+        done, failed = self.status()
+        if failed or done != self.epoch:
+            raise CommTimeoutError(
+                f"rank {self.rank}: cross-GPU sum exchange timed out (last failed call {failed}, "
+                f"last completed {done}, calls made {self.epoch})")
 
     def close(self):
         """Unmaps the peers' workspaces and frees this rank's (after a device synchronize)."""

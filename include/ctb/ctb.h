@@ -161,9 +161,9 @@ CTB_API int ctb_reduce(int op, const ctb_view* in, const ctb_view* out, uint32_t
  * fragmentation and it synchronises the device). Same arguments, results and errors as
  * ctb_reduce; allocates nothing. Split reductions use a fixed 4 MiB array in the library's device
  * image instead (every GPU that loads the library holds it until exit); a reduction that would
- * need more returns CTB_ERR_SCRATCH and names the size. The first call on each device looks up
- * the array's device address (with that device current) and caches it, so make that first call
- * before any stream capture. All calls on a device share the one array and nothing in it needs
+ * need more returns CTB_ERR_SCRATCH and names the size. Each call that needs scratch looks up the
+ * array's address on the current device (the first call on a device also loads the library's
+ * device code there, so make that first call before any stream capture). All calls on a device share the one array and nothing in it needs
  * clearing between calls, but calls that overlap on the GPU (two streams, or two host threads)
  * race on it: serialise them. No counterpart in ctorch (ctorch's CUDA reductions always take
  * scratch from its caching allocator). */
@@ -227,6 +227,17 @@ CTB_API int ctb_peer_alloc(void** d_workspace, void* ipc_handle);
 /* Maps another rank's workspace (from its IPC handle) into this process. */
 CTB_API int ctb_peer_open(const void* ipc_handle, void** d_peer_workspace);
 
+/* Reads this rank's exchange status from its workspace (a synchronous device-to-host copy):
+ * done_epoch = the last call whose exchange completed, failed_epoch = the last call whose wait
+ * for another rank ran out (0: none). */
+CTB_API int ctb_peer_status(const void* d_my_workspace, uint64_t* done_epoch, uint64_t* failed_epoch);
+
+/* Copies this rank's per-call timestamps (a synchronous device-to-host copy) into out[64][4]:
+ * row epoch % 64 holds, in ns of this GPU's %globaltimer, when CTA 0 of that call started, when
+ * its first and its last CTA finished their rows, and when its exchange completed (or its wait
+ * ran out). Rows of calls not yet made are 0. */
+CTB_API int ctb_peer_trace(const void* d_my_workspace, uint64_t* out);
+
 /* Unmaps a workspace opened with ctb_peer_open; frees this rank's own. */
 CTB_API int ctb_peer_close(void* d_peer_workspace);
 CTB_API int ctb_peer_free(void* d_workspace);
@@ -237,9 +248,12 @@ CTB_API int ctb_peer_free(void* d_workspace);
  * addresses, this rank's own at [rank]), waits until every rank's slot in its own workspace
  * carries `epoch`, and writes out_sum (0-d float32/float64) = the rank partials added in rank
  * order, the same on every rank, plus the partials to d_rank_partials [world] when not NULL.
- * Every rank makes the same calls with epoch = 1, 2, 3, ... Each wait is bounded by timeout_ns
- * (0: one second); a wait that runs out is counted (ctb_wait_timeouts) and out_sum is left
- * unwritten. The ranks must run on different GPUs. No ctorch counterpart (ctorch has no
+ * Every rank makes the same calls with epoch = 1, 2, 3, ..., each rank's calls in stream order.
+ * The slots are double-buffered by epoch parity and a slot is taken only when it carries exactly
+ * `epoch`, so a rank that runs one call ahead never feeds a slower rank its next partial. Each
+ * wait is bounded by timeout_ns (0: one second); a wait that runs out is counted
+ * (ctb_wait_timeouts), recorded in the workspace (ctb_peer_status: failed_epoch) and leaves NaN
+ * in out_sum and in the missing ranks' d_rank_partials. The ranks must run on different GPUs. No ctorch counterpart (ctorch has no
  * multi-GPU layer); per rank it is ctb_chain_rows, and the sum is ctorch's whole-tensor sum
  * (src/ops/reduction_ops_cpu.cpp:463) of the row-sharded y. */
 CTB_API int ctb_chain_rows_allsum(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,

@@ -26,6 +26,11 @@ CTB_API int ctb_debug_plan_reduction(const ctb_view* in, const ctb_view* out, ui
 /* floor(n / d) through the kernels' invariant-divisor multiply (n < 2^63, d >= 1). */
 CTB_API uint64_t ctb_debug_fastdiv(uint64_t n, uint64_t d);
 
+/* The size check of ctb_reduce_noalloc, without a device: CTB_OK when a reduction needing `need`
+ * bytes of scratch fits its fixed 4 MiB array, else CTB_ERR_SCRATCH with the message the entry
+ * point gives (ctb_last_error). */
+CTB_API int ctb_debug_noalloc_fits(size_t need);
+
 /* Self-test of the bounded wait (needs a GPU, unlike the functions above): one thread waits on a
  * shared-memory barrier that nothing arrives at, for limit_ns (at most 100 ms), then returns.
  * *completed is 0 when the wait timed out, as it must; the timeout is also counted by

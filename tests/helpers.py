@@ -8,8 +8,8 @@ import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
-# Tolerances written into the tests (SURVEY parity bar; ctorch's own parity tests use the same
-# |g - r| <= tol * max(1, |r|) form, tests/parity/binary_parity_test.cpp:53-69,118-127).
+# Tolerances written into the tests, in the |g - r| <= tol * max(1, |r|) form of ctorch's own
+# parity tests (tests/parity/binary_parity_test.cpp:53-69,118-127).
 TOL_SUM = {np.dtype(np.float32): 1e-5, np.dtype(np.float64): 1e-12}
 # exp/log/tanh/sigmoid: CUDA's accurate math functions vs glibc differ by a few ulp.
 TOL_TRANSCENDENTAL = {np.dtype(np.float32): 2e-6, np.dtype(np.float64): 1e-14}

@@ -5,10 +5,11 @@
   bit-exact, for every dtype, with NaNs and ties that straddle shard boundaries.
 - The one-launch step with the sum exchanged over NVLink (PeerStep / ctb_chain_rows_allsum): a
   world of one against the unfused step, and a world of two with one rank missing, whose bounded
-  wait must run out and be counted.
+  wait must run out, be counted and recorded, and leave NaN as the sum.
 - Two NCCL ranks on two GPUs (skipped with fewer): the sharded sum, the sharded column max/min,
   the one-pass sharded step and the one-launch step, each against the same computation on one GPU
-  or on the NCCL path.
+  or on the NCCL path; and 1000 one-launch steps with the ranks skewed on the host, every sum
+  against the NCCL path's.
 """
 import os
 import socket
@@ -118,6 +119,14 @@ def test_peer_step_on_one_gpu_matches_the_unfused_step(cuda_ok):
         empty = torch.empty(0, 1024, device=dev)
         _, s_empty, _ = peer(empty, r)
         assert s_empty.item() == 0.0
+        peer.check()
+        assert peer.status() == (4, 0)
+        tr = peer.trace()
+        assert tr.shape == (4, 4)
+        assert (tr[:, 0] > 0).all() and (tr[:, 0] <= tr[:, 1]).all() and (tr[:, 1] <= tr[:, 2]).all()
+        assert (tr[:, 2] <= tr[:, 3]).all() and (tr[1:, 0] >= tr[:-1, 3]).all()
+        summary = PeerStep.trace_summary(tr)
+        assert summary["calls"] == 4 and summary["rows_us"] >= 0 and summary["gap_us"] >= 0
     finally:
         peer.close()
     assert C.wait_timeouts() == before
@@ -125,8 +134,8 @@ def test_peer_step_on_one_gpu_matches_the_unfused_step(cuda_ok):
 
 def test_peer_step_with_a_missing_rank_times_out(cuda_ok):
     """A world of two with only one rank: the wait for rank 1's partial (a slot nothing writes)
-    gives up after its 5 ms limit, is counted, leaves the sum unwritten, and the device keeps
-    working."""
+    gives up after its 5 ms limit, is counted and recorded in the workspace, leaves NaN as the sum
+    and as rank 1's partial, and the device keeps working."""
     import ctypes
 
     import torch
@@ -146,14 +155,19 @@ def test_peer_step_with_a_missing_rank_times_out(cuda_ok):
         y = torch.empty_like(x)
         k = torch.empty(64, dtype=torch.int64, device=dev)
         out = torch.full((), -7.0, device=dev)
+        parts = torch.full((2,), -7.0, dtype=torch.float64, device=dev)
         before = C.wait_timeouts()
         rc = C.lib.ctb_chain_rows_allsum(C.SUB, C.MUL, C.view(x), C.view(r), C.view(r), C.view(y), C.MIN,
-                                         C.view(k), peers.data_ptr(), ws.value, 0, 2, 1, C.view(out), None,
-                                         5_000_000, C.stream_handle())
+                                         C.view(k), peers.data_ptr(), ws.value, 0, 2, 1, C.view(out),
+                                         parts.data_ptr(), 5_000_000, C.stream_handle())
         assert rc == C.OK, C.last_error()
         torch.cuda.synchronize()
         assert C.wait_timeouts() == before + 1
-        assert out.item() == -7.0
+        assert torch.isnan(out).item()
+        assert not torch.isnan(parts[0]).item() and torch.isnan(parts[1]).item()
+        done, failed = ctypes.c_uint64(7), ctypes.c_uint64(7)
+        assert C.lib.ctb_peer_status(ws.value, ctypes.byref(done), ctypes.byref(failed)) == C.OK
+        assert (done.value, failed.value) == (0, 1)
         assert torch.equal(y, cb.binary_chain("sub", "mul", x, r, r))  # the step itself still ran
     finally:
         C.lib.ctb_peer_free(ws)
@@ -244,3 +258,75 @@ def test_sharded_layer_on_two_gpus(cuda_ok):
         assert o["peer_ok"], f"rank {r}: the one-launch step differs from the NCCL step"
         assert torch.equal(o["peer_parts"], results[0]["peer_parts"])
         assert o["timeouts"] == 0
+
+
+def _stress_worker(rank, world, port, n_calls, results):
+    """n_calls back-to-back one-launch steps on small shards whose inputs change from call to call
+    (a pool of 5), with host delays between launches on both ranks at different calls, so that
+    each rank in turn runs a call ahead of the other. Every call's sum is kept on the device and
+    compared afterwards with the NCCL path's sum of the same inputs, bit for bit."""
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from ctorch_b200.sharded import PeerStep, ShardedSum, row_shard, sharded_step_fused
+    from ctorch_b200.synth import NORMAL, UNIFORM, device_fill
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        total, cols, pool = 200, 512, 5
+        r = device_fill(torch.empty(1, cols, device=dev), UNIFORM, 21, 1, -1.0, 1.0)
+        sh = row_shard(total, rank, world)
+        xs = [device_fill(torch.empty(total, cols, device=dev), NORMAL, 30 + i, 0, 0.0, 1.0)[sh.start:sh.stop]
+              for i in range(pool)]
+        summer = ShardedSum(dev, world)
+        expect = torch.stack([sharded_step_fused(x, r, summer)[1].clone() for x in xs])
+        peer = PeerStep(dev, rank, world)
+        sums = torch.empty(n_calls, dtype=torch.float32, device=dev)
+        y = torch.empty_like(xs[0])
+        k = torch.empty(xs[0].shape[0], dtype=torch.int64, device=dev)
+        dist.barrier()
+        try:
+            for i in range(n_calls):
+                if (rank == 1 and i % 10 == 3) or (rank == 0 and i % 13 == 7):
+                    torch.cuda.synchronize()
+                    time.sleep(((i * 7919) % 300) * 1e-6)
+                _, s, _ = peer(xs[i % pool], r, y, k)
+                sums[i].copy_(s)
+            torch.cuda.synchronize()
+            status = peer.status()
+        finally:
+            peer.close()
+        want = expect[torch.arange(n_calls, device=dev) % pool]
+        bad = (sums.view(torch.int32) != want.view(torch.int32)).nonzero().flatten()
+        results[rank] = {"bad": bad[:10].cpu().tolist(), "n_bad": int(bad.numel()), "status": status}
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+def test_peer_step_exchange_under_skew_on_two_gpus(cuda_ok):
+    """1000 one-launch steps with the ranks skewed on the host: no call may take another call's
+    partial (every sum equals the NCCL path's for that call's inputs, bit for bit) and every
+    exchange completes."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, n_calls = 2, 1000
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_stress_worker, args=(world, _free_port(), n_calls, results), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
+        o = results[r]
+        assert o["n_bad"] == 0, f"rank {r}: {o['n_bad']} sums differ from the NCCL path, first calls {o['bad']}"
+        assert o["status"] == (n_calls, 0), f"rank {r}: exchange status {o['status']}"

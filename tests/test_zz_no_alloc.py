@@ -97,3 +97,51 @@ def test_reduce_without_allocation_validates_like_ctb_reduce(cuda_ok):
     assert C.lib.ctb_reduce_noalloc(C.MEAN, C.view(x), C.view(bad), 0b10, C.stream_handle()) == C.ERR_DTYPE
     out = torch.empty(4, dtype=torch.int64, device="cuda")
     assert C.lib.ctb_reduce_noalloc(C.SUM, C.view(x), C.view(out), 0b100, C.stream_handle()) == C.ERR_SHAPE
+
+
+_FRESH = r"""
+import ctypes, sys
+sys.path.insert(0, {root!r})
+import torch
+from ctorch_b200 import _capi as C
+
+def run(x, out, mask):
+    rc = C.lib.ctb_reduce_noalloc(C.SUM, C.view(x), C.view(out), mask, C.stream_handle())
+    assert rc == C.OK, C.last_error()
+
+def ref(x, out, mask):
+    need = C.lib.ctb_reduce_scratch_bytes(C.SUM, C.view(x), C.view(out), mask)
+    s = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    rc = C.lib.ctb_reduce(C.SUM, C.view(x), C.view(out), mask, ctypes.c_void_p(s.data_ptr()), need,
+                          C.stream_handle())
+    assert rc == C.OK, C.last_error()
+    return need
+
+g = torch.Generator(device="cuda").manual_seed(99)
+rows = torch.randn(8192, 1024, generator=g, device="cuda")   # row sums: one warp per row, no scratch
+whole = torch.randn(4096, 8192, generator=g, device="cuda")  # whole sum: split, needs scratch
+a, b = torch.empty(8192, device="cuda"), torch.empty(8192, device="cuda")
+assert ref(rows, b, 0b10) == 0
+run(rows, a, 0b10)                       # the first call of the process needs no scratch
+c, d = torch.empty((), device="cuda"), torch.empty((), device="cuda")
+assert ref(whole, d, 0b11) > 0
+run(whole, c, 0b11)                      # the next one does: its address lookup comes now
+torch.cuda.synchronize()
+assert torch.equal(a, b), "row sums differ"
+assert abs(c.item() - d.item()) <= 1e-5 * max(1.0, abs(d.item())), (c.item(), d.item())
+print("fresh ok")
+"""
+
+
+def test_first_call_without_scratch_in_a_fresh_process(cuda_ok):
+    """In a new process whose first no-alloc call needs no scratch (so it skips the array's
+    address lookup), the next call that does need scratch still finds the array: both agree with
+    ctb_reduce."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+    proc = subprocess.run([sys.executable, "-c", _FRESH.format(root=root)], capture_output=True, text=True,
+                          timeout=300)
+    assert proc.returncode == 0 and "fresh ok" in proc.stdout, proc.stdout + proc.stderr
