@@ -235,14 +235,19 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic_per_row():
-    """DRAM bytes (read + write) per row of X for the one-pass kernel, from the committed ncu
-    summary (profiles/ncu_traffic.json), or None."""
+def ncu_traffic(rows):
+    """DRAM bytes (read + write) of one launch of the one-pass kernel over `rows` rows, from the
+    committed ncu capture (profiles/ncu_traffic.json): the read bytes per row times the rows, plus
+    the algorithmic writes per row times the rows, less the constant part of Y still dirty in L2
+    when the kernel ends (which the captured launch did not write back). None if absent."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(p) as f:
             d = json.load(f)
-        return float(d["fused_rows_dram_bytes"]) / float(d["fused_rows_rows"])
+        n = float(d["rows"])
+        read_per_row = float(d["dram_read"]) / n
+        write_per_row = (float(d["dram_write"]) + float(d["l2_write_tail"])) / n
+        return read_per_row * rows + write_per_row * rows - float(d["l2_write_tail"])
     except (OSError, KeyError, ValueError, ZeroDivisionError):
         return None
 
@@ -459,7 +464,7 @@ def run_b200(args):
         peak, peak_kind = measured_peak()
         fused_bytes = shard.rows * COLS * 4 * 2 + COLS * 4 + shard.rows * 8
         achieved = fused_bytes / (fused_ms / 1e3) / 1e9
-        tpr = ncu_traffic_per_row()
+        traffic = ncu_traffic(shard.rows)
         ms_per_step = elapsed / K
         line = {
             "metric": METRIC,
@@ -481,7 +486,9 @@ def run_b200(args):
                          "kernel": "fused_rows_kernel (ctb_chain_rows_allsum: (X - r) * r, row argmin, "
                                    "float64 sum exchanged across ranks in the same launch)",
                          "algorithmic_bytes": fused_bytes,
-                         "traffic": tpr * shard.rows if tpr else None},
+                         "traffic": traffic,
+                         "traffic_note": "ncu DRAM bytes of a 65536-row launch, per row, less the constant "
+                                         "L2 write-back tail (profiles/ncu_traffic.json)"},
             "kernels_ms": {"chain_rows_allsum": fused_ms},
             "step_trace_by_rank": gathered,
             "nccl_step_ms_per_step": nccl_ms,

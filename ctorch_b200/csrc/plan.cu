@@ -415,8 +415,13 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
             if (K * elem_bytes > 8192) {
                 while (plan.row_group < 4 && a.kept * plan.row_group < 6 * warps) plan.row_group *= 2;
             }
+            // as many rounds of rows as a full wave needs, and just enough CTAs for them, so that
+            // the last round is as full as the others
             const int64_t rows_per_cta = 8 / plan.row_group;
-            const int64_t ctas = (a.kept + rows_per_cta - 1) / rows_per_cta;
+            const int64_t wave = slots * rows_per_cta;
+            const int64_t rounds = (a.kept + wave - 1) / wave;
+            const int64_t rows_per_round = (a.kept + rounds - 1) / rounds;
+            const int64_t ctas = (rows_per_round + rows_per_cta - 1) / rows_per_cta;
             plan.grid = static_cast<unsigned>(ctas < slots ? ctas : slots);
             break;
         }

@@ -490,8 +490,10 @@ __device__ __forceinline__ int64_t cols_start(const RedArgs& p, int64_t c) {
 }
 
 template <class R> __global__ void __launch_bounds__(kColsThreads, 1) red_cols_bulk(RedArgs p) {
-    // No allow_dependents() here: red_cols_finalize CTAs resident beside this kernel slowed its
-    // stream (measured); the finalize still launches as a dependent grid once these CTAs exit.
+    // The consumers let the dependent second pass (red_cols_finalize) launch only once they have
+    // folded their last stage: finalize CTAs resident beside this kernel from its start slowed
+    // its stream, while a trigger at the end hides the finalize's launch behind this kernel's
+    // tail (argmax over dim 0 of [8192, 8192] float32 on B200: 52.2 -> 49.6 us for both passes).
     using T = typename R::In;
     using S = typename R::State;
     constexpr int NS = kColsStages;
@@ -597,6 +599,7 @@ template <class R> __global__ void __launch_bounds__(kColsThreads, 1) red_cols_b
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
+        if (pos + (kb - static_cast<int64_t>(ka)) >= end) allow_dependents();
         if (active) {
             const bool whole = ka == 0 && kb == p.K;
             S* part = static_cast<S*>(p.scratch) + (c + static_cast<int64_t>(s)) * TW + t * VE;
@@ -930,8 +933,9 @@ inline bool cols_bulk_ok(const RedPlan& plan, int elem_bytes) {
     if ((a.N * elem_bytes) % 16 || (a.strideK * elem_bytes) % 16) return false;
     for (int d = 0; d < a.rank_k - 1; ++d)
         if ((a.stride_k[d] * elem_bytes) % 16) return false;
-    // at least a quarter of the consumer threads busy; narrower strips go to red_outer
-    if (a.N * elem_bytes < kColsRowBytes / 4) return false;
+    // at least an eighth of the consumer threads busy (rows of 512 B or more); narrower strips
+    // go to red_outer
+    if (a.N * elem_bytes < kColsRowBytes / 8) return false;
     return a.K < (int64_t(1) << 31) - 1;
 }
 

@@ -167,9 +167,10 @@ int registry() {
 //   zero_fill   that zero-fill alone (cudaMemset of the output's bytes), i.e. what an opt-in
 //               uninitialised Storage would take off the front door.
 // `us` is the mean device time per call over `reps` calls back to back between CUDA events on the
-// legacy stream (the stream the backend launches on); `us_sync` is ctorch's own measure, the
-// median host time of one call between two cudaDeviceSynchronize (so it includes the launch
-// latency). Configuration 1's inputs are used as 4 copies in turn (536 MB > the 126 MB L2); the
+// legacy stream (the stream the backend launches on); `host_us` is the host time per call of that
+// loop (when it reaches `us`, the host, not the GPU, sets the pace); `us_sync` is ctorch's own
+// measure, the median host time of one call between two cudaDeviceSynchronize (so it includes
+// the launch latency). Configuration 1's inputs are used as 4 copies in turn (536 MB > the 126 MB L2); the
 // others exceed L2 on their own.
 
 double now_s() {
@@ -183,7 +184,9 @@ template <class F> void time_path(const char* cfg, const char* op, const char* p
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventRecord(e0, cudaStreamLegacy);
+    const double h0 = now_s();
     for (int i = 0; i < reps; ++i) f(i);
+    const double host_us = (now_s() - h0) * 1e6 / reps;
     cudaEventRecord(e1, cudaStreamLegacy);
     cudaEventSynchronize(e1);
     float ms = 0.f;
@@ -202,8 +205,8 @@ template <class F> void time_path(const char* cfg, const char* op, const char* p
     const double us = ms * 1e3 / reps;
     const cudaError_t err = cudaGetLastError();
     std::printf("{\"config\": \"%s\", \"op\": \"%s\", \"path\": \"%s\", \"us\": %.3f, \"us_sync\": %.3f, "
-                "\"gbs\": %.1f, \"algorithmic_bytes\": %.0f, \"reps\": %d, \"cuda\": \"%s\"}\n",
-                cfg, op, path, us, ts[ts.size() / 2] * 1e6, bytes / (us * 1e-6) / 1e9, bytes, reps,
+                "\"host_us\": %.3f, \"gbs\": %.1f, \"algorithmic_bytes\": %.0f, \"reps\": %d, \"cuda\": \"%s\"}\n",
+                cfg, op, path, us, ts[ts.size() / 2] * 1e6, host_us, bytes / (us * 1e-6) / 1e9, bytes, reps,
                 cudaGetErrorString(err));
     std::fflush(stdout);
 }
