@@ -150,6 +150,7 @@ template <class O> struct RowPrep<FnBinary<CTB_DIV, O>> {
 // ------------------------------------------------------------------------------------------------
 template <class Fn, class O, class I0, class I1, class I2, int NIN>
 __global__ void __launch_bounds__(kEwBlock) ew_flat(EwArgs p, Fn fn) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
     constexpr int U = kEwUnroll;
     O* __restrict__ out = static_cast<O*>(p.out);
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(kEwBlock) ew_flat(EwArgs p, Fn fn) {
     const bool b0 = p.stride[1][0] == 0;
     const bool b1 = NIN > 1 && p.stride[2][0] == 0;
     const bool b2 = NIN > 2 && p.stride[3][0] == 0;
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     const I0 s0 = b0 ? in0[0] : I0{};
     I1 s1{};
     I2 s2{};
@@ -296,6 +298,7 @@ template <class O, class I0, class I1, class I2, int NIN, int BMASK> constexpr i
 // whole 8192-float row: about 5% faster there than two tiles of 4 packs a thread).
 template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK, int U, int MINB>
 __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_long(EwArgs p, Fn fn) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     const int64_t seg = static_cast<int64_t>(kEwBlock) * U;
     const int64_t tiles = p.rows * static_cast<int64_t>(p.aux.d);
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -305,6 +308,7 @@ __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_long(EwArgs p, Fn fn) 
         ew_decode_row(p, row, NIN + 1, off);
         ew_row_segment<Fn, O, I0, I1, I2, NIN, BMASK, U>(p, fn, off, static_cast<int64_t>(s) * seg + threadIdx.x,
                                                          kEwBlock, U);
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
@@ -313,6 +317,7 @@ __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_long(EwArgs p, Fn fn) 
 // than per pack. p.aux holds the tiles per row for that U.
 template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK, int U, int MINB>
 __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_mid(EwArgs p, Fn fn) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     constexpr int kWarps = kEwBlock / 32;
     const int64_t seg = 32 * U;
     const int64_t tiles = p.rows * static_cast<int64_t>(p.aux.d);
@@ -324,11 +329,13 @@ __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_mid(EwArgs p, Fn fn) {
         int64_t off[kMaxOps];
         ew_decode_row(p, row, NIN + 1, off);
         ew_row_segment<Fn, O, I0, I1, I2, NIN, BMASK, U>(p, fn, off, static_cast<int64_t>(s) * seg + lane, 32, U);
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
 template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK, int MINB>
 __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_short(EwArgs p, Fn fn) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     constexpr int V = ew_vec<O, I0, I1, I2, NIN>();
     constexpr int U = kEwUnroll;
     bool b0, b1, b2;
@@ -390,12 +397,14 @@ __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_short(EwArgs p, Fn fn)
                 }
             }
         }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
 // ------------------------------------------------------------------------------------------------
 template <class Fn, class O, class I0, class I1, class I2, int NIN>
 __global__ void __launch_bounds__(kEwBlock) ew_general(EwArgs p, Fn fn) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     O* __restrict__ out = static_cast<O*>(p.out);
     const I0* __restrict__ in0 = static_cast<const I0*>(p.in[0]);
     const I1* __restrict__ in1 = static_cast<const I1*>(p.in[1]);
@@ -414,6 +423,7 @@ __global__ void __launch_bounds__(kEwBlock) ew_general(EwArgs p, Fn fn) {
         }
         out[off[0]] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, in0[off[1]], NIN > 1 ? in1[off[2]] : I1{},
                                                        NIN > 2 ? in2[off[3]] : I2{});
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
@@ -423,6 +433,7 @@ __global__ void __launch_bounds__(kEwBlock) ew_general(EwArgs p, Fn fn) {
 // (coalesced), then writes output rows along l (coalesced).
 template <class Fn, class O, class I0, class I1, int XOP>
 __global__ void __launch_bounds__(kEwBlock) ew_tiled(EwArgs p, Fn fn) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     using X = std::conditional_t<XOP == 1, I0, I1>;
     using Y = std::conditional_t<XOP == 1, I1, I0>;
     constexpr int YOP = XOP == 1 ? 2 : 1;
@@ -496,6 +507,7 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled(EwArgs p, Fn fn) {
             }
         }
         __syncthreads();
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
@@ -510,6 +522,7 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled(EwArgs p, Fn fn) {
 // of 256-byte runs spaced a row apart are ~10% slower) at the same bytes in flight per thread.
 template <class Fn, class O, class I0, class I1, int XOP, int TL = kTile>
 __global__ void __launch_bounds__(TL / kTile * kEwBlock) ew_tiled4(EwArgs p, Fn fn) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     using X = std::conditional_t<XOP == 1, I0, I1>;
     using Y = std::conditional_t<XOP == 1, I1, I0>;
     constexpr int YOP = XOP == 1 ? 2 : 1;
@@ -608,6 +621,7 @@ __global__ void __launch_bounds__(TL / kTile * kEwBlock) ew_tiled4(EwArgs p, Fn 
             }
             __syncthreads();
         }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
@@ -642,7 +656,7 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
         const int64_t nvec = a.n / V;
         const int64_t work = (nvec + kEwBlock * kEwUnroll - 1) / (kEwBlock * kEwUnroll);
         auto k = &ew_flat<Fn, O, I0, I1, I2, NIN>;
-        k<<<wave_grid(k, work), kEwBlock, 0, st>>>(a, fn);
+        launch_dependent(k, wave_grid(k, work), kEwBlock, 0, st, a, fn);
         break;
     }
     case EwPath::RowsLong: {
@@ -658,7 +672,7 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
 #define CTB_RL(M, U, B)                                                  \
     {                                                                    \
         auto k = &ew_rows_long<Fn, O, I0, I1, I2, NIN, M, U, B>;         \
-        k<<<wave_grid(k, tiles), kEwBlock, 0, st>>>(al, fn);             \
+        launch_dependent(k, wave_grid(k, tiles), kEwBlock, 0, st, al, fn);             \
     }
 #define CTB_RL2(M)                                                       \
     if constexpr (kWide) {                                               \
@@ -693,7 +707,7 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
 #define CTB_RM(M, B)                                                                             \
     {                                                                                            \
         auto k = &ew_rows_mid<Fn, O, I0, I1, I2, NIN, M, kRowsMidUnroll, B>;                     \
-        k<<<wave_grid(k, work), kEwBlock, 0, st>>>(a, fn);                                       \
+        launch_dependent(k, wave_grid(k, work), kEwBlock, 0, st, a, fn);                                       \
     }
         switch (inner_mask(a, NIN)) {
         case 0: CTB_RM(0, (rows_min_blocks<O, I0, I1, I2, NIN, 0>())) break;
@@ -716,7 +730,7 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
 #define CTB_RS(M, B)                                                     \
     {                                                                    \
         auto k = &ew_rows_short<Fn, O, I0, I1, I2, NIN, M, B>;           \
-        k<<<wave_grid(k, work), kEwBlock, 0, st>>>(a, fn);               \
+        launch_dependent(k, wave_grid(k, work), kEwBlock, 0, st, a, fn);               \
     }
         switch (inner_mask(a, NIN)) {
         case 0: CTB_RS(0, (rows_min_blocks<O, I0, I1, I2, NIN, 0>())) break;
@@ -751,7 +765,7 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
                     const int64_t slots = static_cast<int64_t>(sm_count()) *
                                           resident_ctas(reinterpret_cast<const void*>(k), 2 * kEwBlock);
                     const int64_t g = tw < slots ? tw : slots;
-                    k<<<static_cast<unsigned>(g < 1 ? 1 : g), 2 * kEwBlock, 0, st>>>(aw, fn);
+                    launch_dependent(k, static_cast<unsigned>(g < 1 ? 1 : g), 2 * kEwBlock, 0, st, aw, fn);
                 };
                 if (a.xop == 1) launch(&ew_tiled4<Fn, O, I0, I1, 1, 2 * kTile>);
                 else launch(&ew_tiled4<Fn, O, I0, I1, 2, 2 * kTile>);
@@ -762,22 +776,22 @@ int launch_ew(const EwPlan& plan, Fn fn, cudaStream_t st) {
             } else if (a.tiled_vec) {
                 if (a.xop == 1) {
                     auto k = &ew_tiled4<Fn, O, I0, I1, 1>;
-                    k<<<wave_grid(k, total), kEwBlock, 0, st>>>(a, fn);
+                    launch_dependent(k, wave_grid(k, total), kEwBlock, 0, st, a, fn);
                 } else {
                     auto k = &ew_tiled4<Fn, O, I0, I1, 2>;
-                    k<<<wave_grid(k, total), kEwBlock, 0, st>>>(a, fn);
+                    launch_dependent(k, wave_grid(k, total), kEwBlock, 0, st, a, fn);
                 }
             } else if (a.xop == 1) {
-                ew_tiled<Fn, O, I0, I1, 1><<<grid_for(total, 16), kEwBlock, 0, st>>>(a, fn);
+                launch_dependent(ew_tiled<Fn, O, I0, I1, 1>, grid_for(total, 16), kEwBlock, 0, st, a, fn);
             } else {
-                ew_tiled<Fn, O, I0, I1, 2><<<grid_for(total, 16), kEwBlock, 0, st>>>(a, fn);
+                launch_dependent(ew_tiled<Fn, O, I0, I1, 2>, grid_for(total, 16), kEwBlock, 0, st, a, fn);
             }
             break;
         }
         [[fallthrough]];
     }
     case EwPath::General: {
-        ew_general<Fn, O, I0, I1, I2, NIN><<<grid_for((a.n + kEwBlock - 1) / kEwBlock, 16), kEwBlock, 0, st>>>(a, fn);
+        launch_dependent(ew_general<Fn, O, I0, I1, I2, NIN>, grid_for((a.n + kEwBlock - 1) / kEwBlock, 16), kEwBlock, 0, st, a, fn);
         break;
     }
     }

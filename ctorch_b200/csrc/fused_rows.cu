@@ -147,6 +147,7 @@ template <class T> __device__ __forceinline__ T extreme_ident(bool is_max) {
 // row-broadcast operands.
 template <int OP1, int OP2, class T, int V, bool STAGE, bool RED = true>
 __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     constexpr int U = 4;
     extern __shared__ __align__(16) unsigned char fr_smem[];
     const int lane = threadIdx.x & 31;
@@ -277,6 +278,9 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
             if (lane == 0) p.idx[row * p.idx_stride] = bidx < 0 ? 0 : bidx;
         }
     }
+    // the next kernel in the stream may launch now (it waits for this one to complete before it
+    // touches memory): its launch overlaps this kernel's partial sums and cross-GPU exchange
+    allow_dependents();
     if (RED && p.partials) {
         __shared__ double sm[8];
 #pragma unroll
@@ -314,6 +318,8 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
 
 // Sum of the per-CTA partials (tree_sum_256: the loads overlap, the order is fixed).
 __global__ void __launch_bounds__(256) fused_rows_combine(const double* partials, int n, double* out) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // small kernel: the next one in the stream may launch during it
     __shared__ double sm[8];
     const double t = tree_sum_256(partials, n, sm);
     if (threadIdx.x == 0) *out = t;
@@ -336,15 +342,15 @@ static void launch_typed(bool vec, bool stage, bool red, unsigned grid, size_t s
                          cudaStream_t st) {
     constexpr int V = 16 / sizeof(T);
     if (!red) {
-        fused_rows_kernel<OP1, OP2, T, V, true, false><<<grid, 256, smem, st>>>(p);
+        launch_dependent(fused_rows_kernel<OP1, OP2, T, V, true, false>, grid, 256, smem, st, p);
         return;
     }
     if (stage) {
-        if (vec) fused_rows_kernel<OP1, OP2, T, V, true><<<grid, 256, smem, st>>>(p);
-        else fused_rows_kernel<OP1, OP2, T, 1, true><<<grid, 256, smem, st>>>(p);
+        if (vec) launch_dependent(fused_rows_kernel<OP1, OP2, T, V, true>, grid, 256, smem, st, p);
+        else launch_dependent(fused_rows_kernel<OP1, OP2, T, 1, true>, grid, 256, smem, st, p);
     } else {
-        if (vec) fused_rows_kernel<OP1, OP2, T, V, false><<<grid, 256, 0, st>>>(p);
-        else fused_rows_kernel<OP1, OP2, T, 1, false><<<grid, 256, 0, st>>>(p);
+        if (vec) launch_dependent(fused_rows_kernel<OP1, OP2, T, V, false>, grid, 256, 0, st, p);
+        else launch_dependent(fused_rows_kernel<OP1, OP2, T, 1, false>, grid, 256, 0, st, p);
     }
 }
 
@@ -476,7 +482,7 @@ int fused_rows(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb
     else launch_ops<double>(op1, op2, vec, stage, true, grid, smem, p, st, nullptr);
     int launches = 1;
     if (d_sum) {
-        fused_rows_combine<<<1, 256, 0, st>>>(p.partials, static_cast<int>(grid), d_sum);
+        launch_dependent(fused_rows_combine, 1, 256, 0, st, p.partials, static_cast<int>(grid), d_sum);
         ++launches;
     }
     count_launch(launches);

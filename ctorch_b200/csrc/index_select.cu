@@ -41,6 +41,7 @@ struct GatherArgs {
 
 template <class I>
 __global__ void idx_validate(const I* idx, int64_t n, int64_t stride, int64_t size, int32_t* status) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t i = tid; i < n; i += nthr) {
@@ -49,6 +50,7 @@ __global__ void idx_validate(const I* idx, int64_t n, int64_t stride, int64_t si
             if (atomicCAS(reinterpret_cast<int*>(status), 0, 1) == 0)
                 *reinterpret_cast<long long*>(status + 2) = raw;
         }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
@@ -61,6 +63,7 @@ __device__ __forceinline__ int64_t resolve(const GatherArgs& p, int64_t j) {
 // Warp per output row; U rows in flight per warp; unit VB bytes.
 template <class I, class VT>
 __global__ void __launch_bounds__(256, 4) gather_rows(GatherArgs p) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     constexpr int U = 4;
     constexpr int VB = sizeof(VT);
     if (*reinterpret_cast<volatile int32_t*>(p.status) != 0) return;
@@ -109,11 +112,13 @@ __global__ void __launch_bounds__(256, 4) gather_rows(GatherArgs p) {
                 }
             }
         }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
 template <class I, class ET>
 __global__ void __launch_bounds__(256) gather_general(GatherArgs p) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     if (*reinterpret_cast<volatile int32_t*>(p.status) != 0) return;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -131,6 +136,7 @@ __global__ void __launch_bounds__(256) gather_general(GatherArgs p) {
             rem = q;
         }
         out[oo] = src[so];
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
@@ -154,7 +160,7 @@ int gather_typed(const ctb_view* src, int dim, const ctb_view* idx, const ctb_vi
     if (p.n_idx == 0) return CTB_OK;
     {
         const int64_t blocks = (p.n_idx + 255) / 256;
-        idx_validate<I><<<grid_for(blocks, 8), 256, 0, st>>>(static_cast<const I*>(idx->data), p.n_idx,
+        launch_dependent(idx_validate<I>, grid_for(blocks, 8), 256, 0, st, static_cast<const I*>(idx->data), p.n_idx,
                                                             p.idx_stride, p.dim_size, status);
         count_launch();
         const int rc = check_launch("index_select validate");
@@ -198,11 +204,11 @@ int gather_typed(const ctb_view* src, int dim, const ctb_view* idx, const ctb_vi
         for (int d = 0; d < p.rank_o; ++d) g |= static_cast<uint64_t>(p.stride_o[d] * es);
         const int64_t warps = p.rows;
         const unsigned grid = grid_for((warps + 7) / 8, 16);
-        if ((g & 15u) == 0) gather_rows<I, uint4><<<grid, 256, 0, st>>>(p);
-        else if ((g & 7u) == 0) gather_rows<I, uint2><<<grid, 256, 0, st>>>(p);
-        else if ((g & 3u) == 0) gather_rows<I, uint32_t><<<grid, 256, 0, st>>>(p);
-        else if ((g & 1u) == 0) gather_rows<I, uint16_t><<<grid, 256, 0, st>>>(p);
-        else gather_rows<I, uint8_t><<<grid, 256, 0, st>>>(p);
+        if ((g & 15u) == 0) launch_dependent(gather_rows<I, uint4>, grid, 256, 0, st, p);
+        else if ((g & 7u) == 0) launch_dependent(gather_rows<I, uint2>, grid, 256, 0, st, p);
+        else if ((g & 3u) == 0) launch_dependent(gather_rows<I, uint32_t>, grid, 256, 0, st, p);
+        else if ((g & 1u) == 0) launch_dependent(gather_rows<I, uint16_t>, grid, 256, 0, st, p);
+        else launch_dependent(gather_rows<I, uint8_t>, grid, 256, 0, st, p);
         count_launch();
         return check_launch("index_select gather");
     }
@@ -216,10 +222,10 @@ int gather_typed(const ctb_view* src, int dim, const ctb_view* idx, const ctb_vi
     }
     const unsigned grid = grid_for((n_out + 255) / 256, 16);
     switch (es) {
-    case 1: gather_general<I, uint8_t><<<grid, 256, 0, st>>>(p); break;
-    case 2: gather_general<I, uint16_t><<<grid, 256, 0, st>>>(p); break;
-    case 4: gather_general<I, uint32_t><<<grid, 256, 0, st>>>(p); break;
-    default: gather_general<I, uint64_t><<<grid, 256, 0, st>>>(p); break;
+    case 1: launch_dependent(gather_general<I, uint8_t>, grid, 256, 0, st, p); break;
+    case 2: launch_dependent(gather_general<I, uint16_t>, grid, 256, 0, st, p); break;
+    case 4: launch_dependent(gather_general<I, uint32_t>, grid, 256, 0, st, p); break;
+    default: launch_dependent(gather_general<I, uint64_t>, grid, 256, 0, st, p); break;
     }
     count_launch();
     return check_launch("index_select gather");

@@ -282,7 +282,8 @@ template <class R> __device__ __forceinline__ void fold_contig(const typename R:
 // kernels
 
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_cta(RedArgs p) {
-    allow_dependents();  // a second pass may start its CTAs during this one
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // one-wave grid: the next kernel (a second pass or the next op) may launch now
     using T = typename R::In;
     using S = typename R::State;
     __shared__ S smem[32];
@@ -306,7 +307,8 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_cta(Re
 }
 
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_warp(RedArgs p) {
-    allow_dependents();  // a second pass may start its CTAs during this one
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // one-wave grid: the next kernel (a second pass or the next op) may launch now
     using T = typename R::In;
     using S = typename R::State;
     const int lane = threadIdx.x & 31;
@@ -328,7 +330,8 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_inner_warp(R
 // group's warp results are combined in warp order through shared memory (double-buffered by row
 // parity, one named barrier per row for the group's warps only).
 template <class R, int G> __global__ void __launch_bounds__(kRedBlock) red_inner_group(RedArgs p) {
-    allow_dependents();  // a second pass may start its CTAs during this one
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // one-wave grid: the next kernel (a second pass or the next op) may launch now
     using T = typename R::In;
     using S = typename R::State;
     constexpr int kGroups = kRedBlock / (32 * G);
@@ -358,7 +361,8 @@ template <class R, int G> __global__ void __launch_bounds__(kRedBlock) red_inner
 // Column strips: kept inner dim N contiguous, reduced dim K with stride strideK, batch dims in
 // front. CTA = 8 warps; warp w folds rows k0+w, k0+w+8, ... of a 32*V-column strip.
 template <class R, int V> __global__ void __launch_bounds__(kOuterBlock) red_outer(RedArgs p) {
-    allow_dependents();  // a second pass may start its CTAs during this one
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // one-wave grid: the next kernel (a second pass or the next op) may launch now
     using T = typename R::In;
     using S = typename R::State;
     constexpr int W = kOuterBlock / 32;
@@ -490,6 +494,7 @@ __device__ __forceinline__ int64_t cols_start(const RedArgs& p, int64_t c) {
 }
 
 template <class R> __global__ void __launch_bounds__(kColsThreads, 1) red_cols_bulk(RedArgs p) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     // The consumers let the dependent second pass (red_cols_finalize) launch only once they have
     // folded their last stage: finalize CTAs resident beside this kernel from its start slowed
     // its stream, while a trigger at the end hides the finalize's launch behind this kernel's
@@ -622,6 +627,7 @@ template <class R> __global__ void __launch_bounds__(kColsThreads, 1) red_cols_b
 constexpr int kColsFixGroups = 8;
 template <class R> __global__ void __launch_bounds__(32 * kColsFixGroups) red_cols_finalize(RedArgs p) {
     dependent_wait();  // the first pass has completed and its partials are visible
+    allow_dependents();  // small kernel: the next one in the stream may launch during it
     using T = typename R::In;
     using S = typename R::State;
     constexpr int TW = cols_tile<T>();
@@ -681,7 +687,8 @@ template <class R> __global__ void __launch_bounds__(32 * kColsFixGroups) red_co
 // threads of a column group are then combined in row order through shared memory; the CTA's
 // result is the output, or its split's partial (combined in split order by red_finalize).
 template <class R> __global__ void __launch_bounds__(kNarrowBlock) red_cols_narrow(RedArgs p) {
-    allow_dependents();  // a second pass may start its CTAs during this one
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // one-wave grid: the next kernel (a second pass or the next op) may launch now
     using T = typename R::In;
     using S = typename R::State;
     constexpr int VE = 16 / static_cast<int>(sizeof(T));
@@ -759,7 +766,8 @@ template <class R> __global__ void __launch_bounds__(kNarrowBlock) red_cols_narr
 
 // One thread per output, folding the reduced subspace in row-major order (the CPU's order).
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_thread(RedArgs p) {
-    allow_dependents();  // a second pass may start its CTAs during this one
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // one-wave grid: the next kernel (a second pass or the next op) may launch now
     using T = typename R::In;
     using S = typename R::State;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -776,7 +784,8 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_thre
 
 // CTAs share one output's reduced range (few outputs, long strided reductions).
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_cta(RedArgs p) {
-    allow_dependents();  // a second pass may start its CTAs during this one
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // one-wave grid: the next kernel (a second pass or the next op) may launch now
     using T = typename R::In;
     using S = typename R::State;
     __shared__ S smem[32];
@@ -807,6 +816,7 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_cta(
 // one thread's chain of dependent loads.
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize_cta(RedArgs p) {
     dependent_wait();  // the first pass has completed and its partials are visible
+    allow_dependents();  // small kernel: the next one in the stream may launch during it
     using S = typename R::State;
     __shared__ S smem[kRedBlock / 32];
     const S* part = static_cast<const S*>(p.scratch);
@@ -825,6 +835,7 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize_cta
 // Second pass: combine the `split` partials of each output in split order.
 template <class R> __global__ void __launch_bounds__(kRedBlock) red_finalize(RedArgs p) {
     dependent_wait();  // the first pass has completed and its partials are visible
+    allow_dependents();  // small kernel: the next one in the stream may launch during it
     using S = typename R::State;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -859,23 +870,23 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
     switch (plan.path) {
     case RedPath::Inner:
         if (plan.warp_rows) {
-            if (plan.row_group == 4) red_inner_group<R, 4><<<plan.grid, kRedBlock, 0, st>>>(a);
-            else if (plan.row_group == 2) red_inner_group<R, 2><<<plan.grid, kRedBlock, 0, st>>>(a);
-            else red_inner_warp<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+            if (plan.row_group == 4) launch_dependent(red_inner_group<R, 4>, plan.grid, kRedBlock, 0, st, a);
+            else if (plan.row_group == 2) launch_dependent(red_inner_group<R, 2>, plan.grid, kRedBlock, 0, st, a);
+            else launch_dependent(red_inner_warp<R>, plan.grid, kRedBlock, 0, st, a);
         } else {
-            red_inner_cta<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+            launch_dependent(red_inner_cta<R>, plan.grid, kRedBlock, 0, st, a);
         }
         break;
     case RedPath::Outer: {
         using T = typename R::In;
         if constexpr (sizeof(T) >= 4) {
             if (plan.narrow) {
-                red_cols_narrow<R><<<plan.grid, kNarrowBlock, 0, st>>>(a);
+                launch_dependent(red_cols_narrow<R>, plan.grid, kNarrowBlock, 0, st, a);
                 break;
             }
         }
         if (plan.bulk) {
-            red_cols_bulk<R><<<plan.grid, kColsThreads, cols_smem_bytes(), st>>>(a);
+            launch_dependent(red_cols_bulk<R>, plan.grid, kColsThreads, cols_smem_bytes(), st, a);
             if (int rc = check_launch("reduction")) return rc;
             if (plan.bulk_fixup) {
                 const cudaError_t e = launch_dependent(red_cols_finalize<R>, grid_for((a.kept + 31) / 32, 8),
@@ -886,13 +897,13 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
             break;
         }
         constexpr int VMAX = outer_vec<T>();
-        if (plan.col_tile == 32 * VMAX) red_outer<R, VMAX><<<plan.grid, kOuterBlock, 0, st>>>(a);
-        else red_outer<R, 1><<<plan.grid, kOuterBlock, 0, st>>>(a);
+        if (plan.col_tile == 32 * VMAX) launch_dependent(red_outer<R, VMAX>, plan.grid, kOuterBlock, 0, st, a);
+        else launch_dependent(red_outer<R, 1>, plan.grid, kOuterBlock, 0, st, a);
         break;
     }
     case RedPath::General:
-        if (plan.warp_rows) red_general_thread<R><<<plan.grid, kRedBlock, 0, st>>>(a);
-        else red_general_cta<R><<<plan.grid, kRedBlock, 0, st>>>(a);
+        if (plan.warp_rows) launch_dependent(red_general_thread<R>, plan.grid, kRedBlock, 0, st, a);
+        else launch_dependent(red_general_cta<R>, plan.grid, kRedBlock, 0, st, a);
         break;
     default:
         break;

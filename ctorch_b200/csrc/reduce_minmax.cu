@@ -55,6 +55,8 @@ template <class T, bool IsMax>
 __global__ void minmax_combine_kernel(const T* vals, int64_t vs0, int64_t vs1, const int64_t* idx, int64_t is0,
                                       int64_t is1, const int64_t* offs, int G, int64_t N, T* out_v,
                                       int64_t ov, int64_t* out_i, int64_t oi) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // small kernel: the next one in the stream may launch during it
     using R = RMinMax<T, IsMax, true>;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; n < N; n += nthr) {
@@ -79,12 +81,12 @@ int minmax_combine(int op, const ctb_view* values, const ctb_view* indices, cons
     {                                                                                                      \
         T* ovp = out_values ? static_cast<T*>(out_values->data) : nullptr;                                 \
         if (op == CTB_MAX)                                                                                 \
-            minmax_combine_kernel<T, true><<<grid, 256, 0, st>>>(                                          \
+            launch_dependent(minmax_combine_kernel<T, true>, grid, 256, 0, st,                                           \
                 static_cast<const T*>(values->data), values->strides[0], values->strides[1],               \
                 static_cast<const int64_t*>(indices->data), indices->strides[0], indices->strides[1],      \
                 d_offsets, G, N, ovp, ov, static_cast<int64_t*>(out_indices->data), out_indices->strides[0]); \
         else                                                                                               \
-            minmax_combine_kernel<T, false><<<grid, 256, 0, st>>>(                                         \
+            launch_dependent(minmax_combine_kernel<T, false>, grid, 256, 0, st,                                          \
                 static_cast<const T*>(values->data), values->strides[0], values->strides[1],               \
                 static_cast<const int64_t*>(indices->data), indices->strides[0], indices->strides[1],      \
                 d_offsets, G, N, ovp, ov, static_cast<int64_t*>(out_indices->data), out_indices->strides[0]); \

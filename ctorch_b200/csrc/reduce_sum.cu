@@ -56,6 +56,8 @@ int sum_partial_dispatch(const ctb_view* in, double* d_partial, void* scratch, s
 }
 
 __global__ void sum_combine_kernel(const double* parts, int n, void* out, int dtype) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // small kernel: the next one in the stream may launch during it
     if (blockIdx.x != 0 || threadIdx.x != 0) return;
     double s = 0.0;
     for (int i = 0; i < n; ++i) s = __dadd_rn(s, parts[i]);
@@ -64,7 +66,7 @@ __global__ void sum_combine_kernel(const double* parts, int n, void* out, int dt
 }
 
 int sum_combine(const double* parts, int n, const ctb_view* out, cudaStream_t st) {
-    sum_combine_kernel<<<1, 32, 0, st>>>(parts, n, out->data, out->dtype);
+    launch_dependent(sum_combine_kernel, 1, 32, 0, st, parts, n, out->data, out->dtype);
     count_launch();
     return check_launch("sum_combine");
 }

@@ -16,6 +16,7 @@ __host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
 
 template <class T>
 __global__ void fill_kernel(T* out, int64_t n, int dist, uint64_t key, int64_t first, double lo, double hi) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t i = tid; i < n; i += nthr) {
@@ -38,6 +39,7 @@ __global__ void fill_kernel(T* out, int64_t n, int dist, uint64_t key, int64_t f
             const uint64_t r = range == 0 ? h : h % range;
             out[i] = static_cast<T>(static_cast<int64_t>(static_cast<uint64_t>(a) + r));
         }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
 }
 
@@ -55,14 +57,14 @@ int fill_random(const ctb_view* out, int dist, uint64_t seed, uint64_t stream_id
     const uint64_t key = splitmix64(splitmix64(seed) ^ stream_id);
     const unsigned grid = grid_for((n + 255) / 256, 16);
     switch (out->dtype) {
-    case CTB_FLOAT32: fill_kernel<float><<<grid, 256, 0, st>>>(static_cast<float*>(out->data), n, dist, key, first, lo, hi); break;
-    case CTB_FLOAT64: fill_kernel<double><<<grid, 256, 0, st>>>(static_cast<double*>(out->data), n, dist, key, first, lo, hi); break;
+    case CTB_FLOAT32: launch_dependent(fill_kernel<float>, grid, 256, 0, st, static_cast<float*>(out->data), n, dist, key, first, lo, hi); break;
+    case CTB_FLOAT64: launch_dependent(fill_kernel<double>, grid, 256, 0, st, static_cast<double*>(out->data), n, dist, key, first, lo, hi); break;
     case CTB_INT32:
         if (dist != 0) return fail(CTB_ERR_DTYPE, "normal fill needs a float dtype");
-        fill_kernel<int32_t><<<grid, 256, 0, st>>>(static_cast<int32_t*>(out->data), n, dist, key, first, lo, hi); break;
+        launch_dependent(fill_kernel<int32_t>, grid, 256, 0, st, static_cast<int32_t*>(out->data), n, dist, key, first, lo, hi); break;
     case CTB_INT64:
         if (dist != 0) return fail(CTB_ERR_DTYPE, "normal fill needs a float dtype");
-        fill_kernel<int64_t><<<grid, 256, 0, st>>>(static_cast<int64_t*>(out->data), n, dist, key, first, lo, hi); break;
+        launch_dependent(fill_kernel<int64_t>, grid, 256, 0, st, static_cast<int64_t*>(out->data), n, dist, key, first, lo, hi); break;
     default: return fail(CTB_ERR_DTYPE, "unsupported fill dtype");
     }
     count_launch();
