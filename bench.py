@@ -180,16 +180,21 @@ def run_reference(args):
 # ------------------------------------------------------------------------------- clocks
 
 class ClockSampler:
+    """nvidia-smi clock and throttle-reason samples every 50 ms, each stamped with the host time it
+    arrived, so that stop() keeps only the samples taken inside the timed region."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self):
         self.proc = None
-        self.out = None
+        self.lines = []
+        self.reader = None
 
     def start(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        import threading
+
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
         if vis:
             cmd += ["-i", vis]
@@ -197,19 +202,40 @@ class ClockSampler:
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
 
-    def stop(self):
+        def read():
+            for line in self.proc.stdout:
+                self.lines.append((time.time(), line))
+
+        self.reader = threading.Thread(target=read, daemon=True)
+        self.reader.start()
+
+    def stop(self, t0=None, t1=None):
+        """Median SM clock, max clock and the throttle reasons seen in the samples that arrived
+        between t0 and t1 (host time.time(); all samples when none did, `in_window` false)."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        time.sleep(0.12)  # the sample taken at t1 arrives a little later
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=10)
+            self.proc.wait(timeout=10)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+            self.proc.wait()
+        if self.reader is not None:
+            self.reader.join(timeout=5)
+        lines = self.lines
+        in_window = True
+        if t0 is not None and t1 is not None:
+            sel = [ln for ts, ln in lines if t0 <= ts <= t1 + 0.1]
+            if not sel:
+                sel, in_window = [ln for _, ln in lines], False
+        else:
+            sel = [ln for _, ln in lines]
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for row in csv.reader(io.StringIO(out)):
+        for row in csv.reader(io.StringIO("".join(sel))):
             if len(row) < 9:
                 continue
             try:
@@ -222,7 +248,7 @@ class ClockSampler:
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "in_window": in_window}
 
 
 def measured_peak():
@@ -336,7 +362,11 @@ def run_b200(args):
     barrier()
 
     K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)]
+    # The kernel's own duration (for the roofline) comes from events around every tenth step only:
+    # an event recorded between two launches keeps the second from starting as a programmatic
+    # dependent of the first, so the other steps run back to back as in production.
+    sampled = [i for i in range(K) if i % 10 == 0]
+    ev = {i: [torch.cuda.Event(enable_timing=True) for _ in range(2)] for i in sampled}
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler()
     if rank == 0:
@@ -345,16 +375,20 @@ def run_b200(args):
     barrier()
     torch.cuda.synchronize()
     cb.launch_count_reset()
+    t_region0 = time.time()
     start.record()
     for i in range(K):
-        ev[i][0].record()
+        if i in ev:
+            ev[i][0].record()
         step()
-        ev[i][1].record()
+        if i in ev:
+            ev[i][1].record()
     end.record()
     torch.cuda.synchronize()
+    t_region1 = time.time()
     barrier()
     launches = cb.launch_count()
-    clocks = sampler.stop() if rank == 0 else None
+    clocks = sampler.stop(t_region0, t_region1) if rank == 0 else None
     check_exchange()
     # where a step's time goes on each rank (kernel-side timestamps of the last timed calls)
     step_trace = PeerStep.trace_summary(peer.trace(min(K, 64)))
@@ -364,7 +398,7 @@ def run_b200(args):
     else:
         gathered = [step_trace]
     elapsed = max_over_ranks(start.elapsed_time(end))
-    fused_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in ev))
+    fused_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in ev.values()))
     total_launches = int(sum_over_ranks(launches))
 
     def time_steps(fn, n):
@@ -489,7 +523,9 @@ def run_b200(args):
                          "traffic": traffic,
                          "traffic_note": "ncu DRAM bytes of a 65536-row launch, per row, less the constant "
                                          "L2 write-back tail (profiles/ncu_traffic.json)"},
-            "kernels_ms": {"chain_rows_allsum": fused_ms},
+            "kernels_ms": {"chain_rows_allsum": fused_ms,
+                           "timed_launches": len(ev),
+                           "note": "CUDA events around every tenth timed step, max over ranks of the mean"},
             "step_trace_by_rank": gathered,
             "nccl_step_ms_per_step": nccl_ms,
             "three_kernel_ms_per_step": three_kernel_ms,
@@ -584,10 +620,10 @@ def run_suite(args, sink=None):
     """Per-op device time and GB/s for every op of the five configurations, one JSON line per op
     (appended to `sink` instead when it is a list: the default run's `per_op` key).
 
-    Each op (or, for configuration 1, whose working set is about the size of L2, a round of the op
-    on 4 separate copies of its inputs) is captured in a CUDA graph and replayed `--steps` times
-    back to back between CUDA events on the replay stream; the op's time is the elapsed time per
-    call. The inputs touched between two calls on the same data exceed the 126 MB L2, so no flush
+    Each op is captured 8 times back to back in a CUDA graph (configuration 1, whose working set is
+    about the size of L2, as 2 rounds over 4 separate copies of its inputs), and the graph is
+    replayed `--steps` times back to back between CUDA events on the replay stream; the op's time
+    is the elapsed time per call, each call following another as in a stream of eager ops. The inputs touched between two calls on the same data exceed the 126 MB L2, so no flush
     is needed, and no host (Python / ctypes) time falls inside the measurement. ctorch's own CPU
     path (oracle/_ref, its public front-doors, one thread) is timed on the same inputs, or on a
     stated sample of them, unless --no-cpu-baseline is given."""
@@ -608,6 +644,9 @@ def run_suite(args, sink=None):
         ref = get_ref()
 
     def graph_ms(fns):
+        # 8 calls per graph (rounds of fns), so that each call follows another as in a stream of
+        # eager ops: every kernel is launched as a programmatic dependent of the one before it
+        fns = list(fns) * max(1, 8 // len(fns))
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
