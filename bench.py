@@ -593,6 +593,21 @@ def run_case(args):
     elif case == "cols_outer":  # rows of 8190 floats (not a whole number of 16-byte chunks): the register kernel
         x = device_fill(t((8192, 8190)), NORMAL, 1, 0, 0.0, 1.0)
         fn = lambda: cb.max(x, 0)  # noqa: E731
+    elif case == "rows_short":  # rows of 64 floats with a broadcast row: the short-row elementwise kernel
+        a = device_fill(t((1_048_576, 64)), UNIFORM, 0, 0, -1.0, 1.0)
+        b = device_fill(t((1, 64)), UNIFORM, 0, 1, -1.0, 1.0)
+        fn = lambda: cb.add(a, b)  # noqa: E731
+    elif case == "tiled_f64":  # float64 operand read transposed: the 64x64 shared-memory tile kernel
+        a = device_fill(t((32, 1024, 1024), torch.float64), UNIFORM, 3, 0, -1.0, 1.0)
+        b = device_fill(t((32, 1024, 1024), torch.float64), UNIFORM, 3, 1, -1.0, 1.0)
+        fn = lambda: cb.mul(a, b.permute(0, 2, 1))  # noqa: E731
+    elif case == "ew_general":  # two operands permuted two different ways: the per-element decode kernel
+        a = device_fill(t((1024, 1024, 64)), UNIFORM, 3, 0, -1.0, 1.0)
+        b = device_fill(t((64, 1024, 1024)), UNIFORM, 3, 1, -1.0, 1.0)
+        fn = lambda: cb.add(a.permute(2, 0, 1), b.transpose(1, 2))  # noqa: E731
+    elif case == "red_general":  # sum over dims 0 and 2 of [64, 1024, 1024]: the general reduction
+        x = device_fill(t((64, 1024, 1024)), NORMAL, 1, 0, 0.0, 1.0)
+        fn = lambda: cb.sum(x, [0, 2])  # noqa: E731
     elif case == "argmin_rows":
         y = device_fill(t((rows, COLS)), NORMAL, SEED, 0, 0.0, 1.0)
         fn = lambda: cb.argmin(y, 1)  # noqa: E731
@@ -797,7 +812,8 @@ def main():
     ap.add_argument("--case", default=None,
                     help="profiling mode: launch one kernel (chain_rows, chain, sub, sum, argmin, step, add, relu, "
                          "sum_rows, prod_rows, argmax_cols, max_cols, sum_cols, cols_narrow, cols_outer, argmin_rows, "
-                         "index_select, mul_t, div_b) --warmup + --steps times")
+                         "rows_short, tiled_f64, ew_general, red_general, index_select, mul_t, div_b) --warmup + --steps "
+                         "times")
     ap.add_argument("--rows", type=int, default=16384, help="rows of X for --case (default 16384: 512 MiB)")
     ap.add_argument("--suite", action="store_true",
                     help="per-op device time, GB/s and ctorch CPU time for every op of the five configurations")
