@@ -174,3 +174,22 @@ def test_sharded_index_select_covers_all_rows():
     idx = torch.tensor([3, 1, 4, 1, 5, 9, 2, 6, 5])
     parts = [sharded_index_select(table, idx, len(idx), r, 4, select=torch.index_select) for r in range(4)]
     assert torch.equal(torch.cat(parts), table[idx])
+
+
+def test_peer_trace_summary():
+    """PeerStep.trace_summary on hand-made timestamps (ns): per call (CTA 0 start, first CTA done,
+    last CTA done, exchange complete); medians in microseconds, the launch gap between calls."""
+    import numpy as np
+
+    from ctorch_b200.sharded import PeerStep
+
+    tr = np.array([[0, 9_000, 10_000, 10_500],
+                   [12_500, 20_000, 22_500, 23_000],
+                   [25_000, 33_000, 35_000, 36_000]], dtype=np.int64)
+    s = PeerStep.trace_summary(tr)
+    assert s["calls"] == 3
+    assert s["rows_us"] == 10.0          # median of 10, 10, 10
+    assert s["tail_us"] == 2.0           # median of 1, 2.5, 2
+    assert s["exchange_us"] == 0.5       # median of 0.5, 0.5, 1
+    assert s["gap_us"] == 2.0            # median of 2, 2
+    assert PeerStep.trace_summary(np.zeros((0, 4), np.int64)) == {}
