@@ -186,18 +186,21 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self):
+    def __init__(self, n_devices=1):
+        self.n_devices = n_devices
         self.proc = None
         self.lines = []
         self.reader = None
 
     def start(self):
+        """Samples the GPUs the job's ranks use (local ranks 0..n-1 on devices 0..n-1 of the
+        visible list), not the node's other GPUs, which may be idle."""
         import threading
 
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-        if vis:
-            cmd += ["-i", vis]
+        ids = vis.split(",")[: self.n_devices] if vis else [str(i) for i in range(self.n_devices)]
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+               "-i", ",".join(i.strip() for i in ids)]
         try:
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
@@ -368,7 +371,7 @@ def run_b200(args):
     sampled = [i for i in range(K) if i % 10 == 0]
     ev = {i: [torch.cuda.Event(enable_timing=True) for _ in range(2)] for i in sampled}
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler()
+    sampler = ClockSampler(int(os.environ.get("LOCAL_WORLD_SIZE", world)))
     if rank == 0:
         sampler.start()
         time.sleep(0.3)
@@ -605,8 +608,11 @@ def run_case(args):
         a = device_fill(t((1024, 1024, 64)), UNIFORM, 3, 0, -1.0, 1.0)
         b = device_fill(t((64, 1024, 1024)), UNIFORM, 3, 1, -1.0, 1.0)
         fn = lambda: cb.add(a.permute(2, 0, 1), b.transpose(1, 2))  # noqa: E731
-    elif case == "red_general":  # sum over dims 0 and 2 of [64, 1024, 1024]: the general reduction
+    elif case == "red_runs":  # sum over dims 0 and 2 of [64, 1024, 1024]: packs along the reduced runs
         x = device_fill(t((64, 1024, 1024)), NORMAL, 1, 0, 0.0, 1.0)
+        fn = lambda: cb.sum(x, [0, 2])  # noqa: E731
+    elif case == "red_general":  # the same over [64, 1024, 1023]: runs of 1023 floats, per-element decode
+        x = device_fill(t((64, 1024, 1023)), NORMAL, 1, 0, 0.0, 1.0)
         fn = lambda: cb.sum(x, [0, 2])  # noqa: E731
     elif case == "argmin_rows":
         y = device_fill(t((rows, COLS)), NORMAL, SEED, 0, 0.0, 1.0)
@@ -812,7 +818,7 @@ def main():
     ap.add_argument("--case", default=None,
                     help="profiling mode: launch one kernel (chain_rows, chain, sub, sum, argmin, step, add, relu, "
                          "sum_rows, prod_rows, argmax_cols, max_cols, sum_cols, cols_narrow, cols_outer, argmin_rows, "
-                         "rows_short, tiled_f64, ew_general, red_general, index_select, mul_t, div_b) --warmup + --steps "
+                         "rows_short, tiled_f64, ew_general, red_runs, red_general, index_select, mul_t, div_b) --warmup + --steps "
                          "times")
     ap.add_argument("--rows", type=int, default=16384, help="rows of X for --case (default 16384: 512 MiB)")
     ap.add_argument("--suite", action="store_true",

@@ -395,6 +395,7 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
     plan.narrow = false;
     plan.row_group = 1;
     plan.bulk_fixup = false;
+    plan.runs = false;
     a.split = 1;
     a.chunk = a.red;
     a.sk_q = a.sk_r = 0;
@@ -528,16 +529,29 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
         const int64_t slots = sms * occ.general_cta;
         // few outputs with long reduced ranges: CTAs share an output; otherwise one thread each
         if (a.kept < slots * 32 && a.red >= 1024) {
-            int64_t split = std::max<int64_t>(1, slots / a.kept);
+            // contiguous innermost reduced dim, whole packs per run, runs on 16-byte boundaries:
+            // red_runs_cta (chunks counted in packs) instead of the per-element decode
+            const int vec = 16 / elem_bytes;
+            const int64_t run = a.rank_r > 0 ? a.shape_r[a.rank_r - 1] : 0;
+            const int64_t rslots = sms * occ.runs;
+            bool runs = occ.runs > 0 && a.rank_r > 0 && a.stride_r[a.rank_r - 1] == 1 &&
+                        run % vec == 0 && run >= 4 * vec && reinterpret_cast<uintptr_t>(a.in) % 16 == 0;
+            for (int d = 0; runs && d < a.rank_k; ++d) runs = (a.stride_k[d] * elem_bytes) % 16 == 0;
+            for (int d = 0; runs && d + 1 < a.rank_r; ++d) runs = (a.stride_r[d] * elem_bytes) % 16 == 0;
+            const int64_t units = runs ? a.red / vec : a.red;  // packs or elements
+            const int64_t use_slots = runs ? rslots : slots;
+            int64_t split = std::max<int64_t>(1, use_slots / a.kept);
             split = std::min<int64_t>(split, std::max<int64_t>(1, a.red / 4096));
-            const int64_t chunk = (a.red + split - 1) / split;
-            split = (a.red + chunk - 1) / chunk;
+            const int64_t chunk = (units + split - 1) / split;
+            split = (units + chunk - 1) / chunk;
             a.split = static_cast<int>(split);
             a.chunk = chunk;
             a.aux = FastDiv(static_cast<uint64_t>(split));
+            if (runs) a.aux2 = FastDiv(static_cast<uint64_t>(run / vec));
+            plan.runs = runs;
             plan.warp_rows = false;
             const int64_t work = a.kept * split;
-            plan.grid = static_cast<unsigned>(work < slots ? work : slots);
+            plan.grid = static_cast<unsigned>(work < use_slots ? work : use_slots);
             if (split > 1) scratch = static_cast<size_t>(a.kept * split) * state_bytes;
         } else {
             plan.warp_rows = true;  // here: one thread per output

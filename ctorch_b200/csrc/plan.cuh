@@ -128,6 +128,8 @@ struct RedPlan {
     bool bulk = false;       // Outer: bulk-copy column kernel (red_cols_bulk) instead of red_outer
     bool narrow = false;     // Outer: contiguous narrow rows (red_cols_narrow) instead of red_outer
     bool bulk_fixup = false; // bulk: some column tile is shared by several CTAs (second pass)
+    bool runs = false;       // General, CTA per output: the innermost reduced dim is contiguous and
+                             // pack-aligned, so red_runs_cta streams 16-byte packs along its runs
     int64_t bulk_tiles = 0;  // bulk: column tiles
 };
 
@@ -144,6 +146,7 @@ struct RedOcc {
     int inner_cta = 4, inner_warp = 4, outer = 4, general_cta = 4;
     int cols_bulk = 0;  // resident bulk column CTAs per SM; 0 when that kernel cannot take the plan
     int cols_narrow = 0;  // resident narrow-column CTAs per SM; 0 when that kernel cannot take it
+    int runs = 0;         // resident red_runs_cta CTAs per SM; 0 when that kernel cannot take the plan
 };
 
 // Narrow column kernel: 256 threads, each owning one 16-byte column group of a contiguous

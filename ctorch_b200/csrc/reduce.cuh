@@ -7,6 +7,8 @@
 //   red_inner_warp  same for short rows: one warp per row
 //   red_outer       reduced dim strided, kept dim contiguous (column reductions): each warp walks
 //                   rows of a 32*V-column strip, warps combine through shared memory
+//   red_runs_cta    other layouts whose innermost reduced dim is contiguous: 16-byte packs along
+//                   the runs, each pack's run decoded once
 //   red_general_*   any other layout: per-element coordinate decode
 //   red_finalize    deterministic fixed-order combine of split partials (the second pass);
 //                   red_finalize_cta for few outputs with many partials (a CTA-wide fixed tree)
@@ -809,6 +811,66 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_general_cta(
     }
 }
 
+// CTAs share one output's reduced range, whose innermost reduced dim is contiguous (runs of
+// shape_r[rank_r - 1] elements, a whole number of 16-byte packs, every run on a 16-byte
+// boundary): e.g. a sum over dims 0 and 2 of [64, 1024, 1024]. The output's runs are one sequence
+// of packs (aux2 = packs per run); thread t takes packs t, t + 256, ... with 4 in flight,
+// decoding each pack's run once, so every load is a 16-byte pack and a warp reads 512 contiguous
+// bytes of a run. Each thread folds its elements in increasing position, so the first-index and
+// first-NaN rules hold within it and block_reduce combines the threads by position. p.chunk
+// counts packs per split.
+template <class R> __global__ void __launch_bounds__(kRedBlock) red_runs_cta(RedArgs p) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    allow_dependents();  // one-wave grid: the next kernel (a second pass or the next op) may launch now
+    using T = typename R::In;
+    using S = typename R::State;
+    constexpr int V = 16 / static_cast<int>(sizeof(T));
+    constexpr int U = 4;
+    __shared__ S smem[32];
+    const T* in = static_cast<const T*>(p.in);
+    const int64_t L = p.shape_r[p.rank_r - 1];
+    const int64_t npacks = p.red / V;
+    const int64_t total = p.kept * p.split;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        uint64_t k, sp;
+        p.aux.divmod(static_cast<uint64_t>(t), k, sp);
+        int64_t in_off, o1, o2;
+        red_decode_kept(p, k, in_off, o1, o2);
+        const int64_t q0 = static_cast<int64_t>(sp) * p.chunk;
+        const int64_t q1 = q0 + p.chunk < npacks ? q0 + p.chunk : npacks;
+        S st = R::init();
+        for (int64_t q = q0 + threadIdx.x; q < q1; q += static_cast<int64_t>(blockDim.x) * U) {
+            Pack<T, V> x[U];
+            int64_t pos[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t qq = q + static_cast<int64_t>(u) * blockDim.x;
+                if (qq < q1) {
+                    uint64_t r, c;
+                    p.aux2.divmod(static_cast<uint64_t>(qq), r, c);
+                    const int64_t j = static_cast<int64_t>(r) * L;  // first position of the run
+                    pos[u] = j + static_cast<int64_t>(c) * V;
+                    x[u] = load_pack<T, V>(in + in_off + red_decode_red(p, static_cast<uint64_t>(j)) +
+                                           static_cast<int64_t>(c) * V);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t qq = q + static_cast<int64_t>(u) * blockDim.x;
+                if (qq < q1) {
+#pragma unroll
+                    for (int e = 0; e < V; ++e) R::fold(st, x[u].v[e], pos[u] + e);
+                }
+            }
+        }
+        st = block_reduce<R>(st, smem);
+        if (threadIdx.x == 0) {
+            if (p.split == 1) R::write(p, st, o1, o2);
+            else static_cast<S*>(p.scratch)[t] = st;
+        }
+    }
+}
+
 // Second pass for few outputs with many partials each (a whole-tensor sum split over every SM):
 // one CTA per output; thread t folds partials t, t + 256, ... in order, then a fixed-shape tree
 // (warp shuffles, then the warps' results) combines the threads. The shape depends only on the
@@ -903,6 +965,7 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
     }
     case RedPath::General:
         if (plan.warp_rows) launch_dependent(red_general_thread<R>, plan.grid, kRedBlock, 0, st, a);
+        else if (plan.runs) launch_dependent(red_runs_cta<R>, plan.grid, kRedBlock, 0, st, a);
         else launch_dependent(red_general_cta<R>, plan.grid, kRedBlock, 0, st, a);
         break;
     default:
@@ -1013,6 +1076,7 @@ int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint
     occ.outer = vec_ok ? resident_ctas(reinterpret_cast<const void*>(&red_outer<R, V>), kOuterBlock)
                        : resident_ctas(reinterpret_cast<const void*>(&red_outer<R, 1>), kOuterBlock);
     occ.general_cta = resident_ctas(reinterpret_cast<const void*>(&red_general_cta<R>), kRedBlock);
+    occ.runs = resident_ctas(reinterpret_cast<const void*>(&red_runs_cta<R>), kRedBlock);
     need = finish_reduction_plan(plan, sizeof(T), sizeof(typename R::State), vec_ok ? V : 1, occ);
     return CTB_OK;
 }

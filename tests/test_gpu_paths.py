@@ -258,6 +258,12 @@ RED_LAYOUTS = {
     "outer_transposed": ((700, 900), [("permute", [1, 0])], [1], False),
     "general_cta": ((1500, 1200), [("permute", [1, 0]), ("slice", 0, 0, 1200, 2)], None, False),
     "general_thread": ((60, 7, 90), [], [0, 2], False),
+    # reduced dims that do not collapse, the innermost contiguous and pack-aligned: red_runs_cta
+    "general_runs": ((40, 300, 512), [], [0, 2], False),
+    "general_runs_split_keepdim": ((8, 2, 6, 4096), [], [1, 3], True),
+    "general_runs_batch_offset": ((3, 20, 50, 1024), [("slice", 0, 1, 3, 1)], [1, 3], False),
+    # the same with rows of 513 elements cut to 512: runs no longer start on 16-byte boundaries
+    "general_runs_unaligned": ((40, 300, 513), [("slice", 2, 0, 512, 1)], [0, 2], False),
 }
 
 
