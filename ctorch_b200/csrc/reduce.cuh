@@ -246,6 +246,20 @@ __device__ __forceinline__ int64_t red_decode_red(const RedArgs& p, uint64_t j) 
     return off;
 }
 
+// Offset of run r of the reduced subspace whose innermost dim (rank_r - 1) is contiguous: r
+// decoded over the outer reduced dims only, the outermost without a divide (its coordinate is
+// what is left). Two reduced dims cost one multiply.
+__device__ __forceinline__ int64_t red_decode_run(const RedArgs& p, uint64_t r) {
+    int64_t off = 0;
+    for (int d = p.rank_r - 2; d > 0; --d) {
+        uint64_t q, c;
+        p.div_r[d].divmod(r, q, c);
+        off += static_cast<int64_t>(c) * p.stride_r[d];
+        r = q;
+    }
+    return off + static_cast<int64_t>(r) * p.stride_r[0];
+}
+
 // Folds row[j] for j in [j0, j1) into s, elements spread over nthr threads: scalar head up to
 // the first 16-byte boundary, 16-byte packs R::kUnroll deep, scalar tail.
 template <class R> __device__ __forceinline__ void fold_contig(const typename R::In* row, int64_t j0,
@@ -850,8 +864,7 @@ template <class R> __global__ void __launch_bounds__(kRedBlock) red_runs_cta(Red
                     p.aux2.divmod(static_cast<uint64_t>(qq), r, c);
                     const int64_t j = static_cast<int64_t>(r) * L;  // first position of the run
                     pos[u] = j + static_cast<int64_t>(c) * V;
-                    x[u] = load_pack<T, V>(in + in_off + red_decode_red(p, static_cast<uint64_t>(j)) +
-                                           static_cast<int64_t>(c) * V);
+                    x[u] = load_pack<T, V>(in + in_off + red_decode_run(p, r) + static_cast<int64_t>(c) * V);
                 }
             }
 #pragma unroll
