@@ -94,10 +94,10 @@ __device__ void allsum_epilogue(const FusedRowsArgs& p) {
     const int g = threadIdx.x;
     const int par = static_cast<int>(p.epoch & 1u);
     if (g < p.world) {
-        // publish: value, then (after a system-scope fence) the epoch that marks it valid
+        // publish: value, then the epoch that marks it valid, as a system-scope release store (it
+        // orders this thread's value store before it for every observer, the peers included)
         PeerSlot* dst = &p.peers[g]->slots[par][p.rank];
         *reinterpret_cast<volatile double*>(&dst->value) = mine_sh;
-        __threadfence_system();
         st_release_sys(&dst->epoch, p.epoch);
     }
     if (g < p.world) {
