@@ -617,6 +617,10 @@ def run_case(args):
     elif case == "argmin_rows":
         y = device_fill(t((rows, COLS)), NORMAL, SEED, 0, 0.0, 1.0)
         fn = lambda: cb.argmin(y, 1)  # noqa: E731
+    elif case == "gather_general":  # rows gathered from a transposed source: the strided gather kernel
+        x = device_fill(t((8192, 8192)), NORMAL, 2, 0, 0.0, 1.0)
+        idx = device_fill(t((4096,), torch.int64), UNIFORM, 2, 2, 0, 8191)
+        fn = lambda: cb.index_select_async(x.t(), 0, idx)  # noqa: E731
     elif case == "index_select":
         tab = device_fill(t((1_000_000, 256)), NORMAL, 2, 0, 0.0, 1.0)
         idx = device_fill(t((rows * 16,), torch.int64), UNIFORM, 2, 2, 0, 999_999)
@@ -818,7 +822,7 @@ def main():
     ap.add_argument("--case", default=None,
                     help="profiling mode: launch one kernel (chain_rows, chain, sub, sum, argmin, step, add, relu, "
                          "sum_rows, prod_rows, argmax_cols, max_cols, sum_cols, cols_narrow, cols_outer, argmin_rows, "
-                         "rows_short, tiled_f64, ew_general, red_runs, red_general, index_select, mul_t, div_b) --warmup + --steps "
+                         "rows_short, tiled_f64, ew_general, red_runs, red_general, gather_general, index_select, mul_t, div_b) --warmup + --steps "
                          "times")
     ap.add_argument("--rows", type=int, default=16384, help="rows of X for --case (default 16384: 512 MiB)")
     ap.add_argument("--suite", action="store_true",
