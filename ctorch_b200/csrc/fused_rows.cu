@@ -145,10 +145,7 @@ template <class T> __device__ __forceinline__ T extreme_ident(bool is_max) {
 // loads of a; without STAGE (rows too long for shared memory) they are read through L1.
 // RED = false: the chain alone (y only; no row extreme, no sum), for ctb_binary_chain on
 // row-broadcast operands.
-// MAX: the row extreme is the maximum (else the minimum), fixed at compile time so that each
-// element costs one ordered compare and the NaN guard (a runtime direction issued both compares
-// and a select: 1.6% slower over 2000 back-to-back launches in a standalone copy of this loop).
-template <int OP1, int OP2, class T, int V, bool STAGE, bool RED = true, bool MAX = false>
+template <int OP1, int OP2, class T, int V, bool STAGE, bool RED = true>
 __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
     dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
     constexpr int U = 4;
@@ -197,9 +194,7 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
     const bool c_row = STAGE || !p.c_bcast;
     const T* __restrict__ A = static_cast<const T*>(p.a);
     T* __restrict__ Y = static_cast<T*>(p.y);
-    // staged rows: when c is b, Cc already points at b's staged row, so the loop reads it there
-    // instead of choosing per element
-    const bool cib = !STAGE && p.c_is_b;
+    const bool is_max = p.is_max != 0;
     const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
     const int nv = C / V;  // whole packs per row (V == 1 when rows are not pack-aligned)
@@ -208,7 +203,7 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
     for (int64_t row = warp; row < p.rows; row += nwarps) {
         const T* ar = A + row * p.a_row_stride;
         T* yr = Y ? Y + row * p.y_row_stride : nullptr;
-        T best = extreme_ident<T>(MAX);
+        T best = extreme_ident<T>(is_max);
         int bidx = -1;
         for (int v0 = lane; v0 < nv; v0 += 32 * U) {
             Pack<T, V> xa[U];
@@ -223,16 +218,16 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
                 if (v < nv) {
                     Pack<T, V> xb, xc, o;
                     if (b_row) xb = *reinterpret_cast<const Pack<T, V>*>(B + v * V);
-                    if (!cib && c_row) xc = *reinterpret_cast<const Pack<T, V>*>(Cc + v * V);
+                    if (!p.c_is_b && c_row) xc = *reinterpret_cast<const Pack<T, V>*>(Cc + v * V);
 #pragma unroll
                     for (int e = 0; e < V; ++e) {
                         const T bb = b_row ? xb.v[e] : B[0];
-                        const T cc = cib ? bb : (c_row ? xc.v[e] : Cc[0]);
+                        const T cc = p.c_is_b ? bb : (c_row ? xc.v[e] : Cc[0]);
                         const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(xa[u].v[e], bb), cc);
                         o.v[e] = yv;
                         if constexpr (RED) {
                             sum = __dadd_rn(sum, static_cast<double>(yv));
-                            const bool repl = (best == best) && !(MAX ? yv <= best : yv >= best);
+                            const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
                             if (repl) {
                                 best = yv;
                                 bidx = v * V + e;
@@ -246,12 +241,12 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
         // scalar tail (columns past the last whole pack)
         for (int j = nv * V + lane; j < C; j += 32) {
             const T bb = b_row ? B[j] : B[0];
-            const T cc = cib ? bb : (c_row ? Cc[j] : Cc[0]);
+            const T cc = p.c_is_b ? bb : (c_row ? Cc[j] : Cc[0]);
             const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(ar[j], bb), cc);
             if (yr) yr[j] = yv;
             if constexpr (RED) {
                 sum = __dadd_rn(sum, static_cast<double>(yv));
-                const bool repl = (best == best) && !(MAX ? yv <= best : yv >= best);
+                const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
                 if (repl) {
                     best = yv;
                     bidx = j;
@@ -271,7 +266,7 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
                 else {
                     const bool an = best != best, bn = ov != ov;
                     if (an || bn) take = an ? (bn && oi < bidx) : true;
-                    else if (MAX ? ov > best : ov < best) take = true;
+                    else if (is_max ? ov > best : ov < best) take = true;
                     else take = (ov == best) && oi < bidx;
                 }
                 if (take) {
@@ -330,33 +325,15 @@ __global__ void __launch_bounds__(256) fused_rows_combine(const double* partials
     if (threadIdx.x == 0) *out = t;
 }
 
-template <int OP1, int OP2, class T, bool MAX>
-static const void* pick_red(bool vec, bool stage) {
-    constexpr int V = 16 / sizeof(T);
-    if (stage)
-        return vec ? reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, true, true, MAX>)
-                   : reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, 1, true, true, MAX>);
-    return vec ? reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, false, true, MAX>)
-               : reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, 1, false, true, MAX>);
-}
-
 template <int OP1, int OP2, class T>
-static const void* pick_kernel(bool vec, bool stage, bool red, bool is_max) {
+static const void* pick_kernel(bool vec, bool stage, bool red) {
     constexpr int V = 16 / sizeof(T);
     if (!red) return reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, true, false>);
-    return is_max ? pick_red<OP1, OP2, T, true>(vec, stage) : pick_red<OP1, OP2, T, false>(vec, stage);
-}
-
-template <int OP1, int OP2, class T, bool MAX>
-static void launch_red(bool vec, bool stage, unsigned grid, size_t smem, const FusedRowsArgs& p, cudaStream_t st) {
-    constexpr int V = 16 / sizeof(T);
-    if (stage) {
-        if (vec) launch_dependent(fused_rows_kernel<OP1, OP2, T, V, true, true, MAX>, grid, 256, smem, st, p);
-        else launch_dependent(fused_rows_kernel<OP1, OP2, T, 1, true, true, MAX>, grid, 256, smem, st, p);
-    } else {
-        if (vec) launch_dependent(fused_rows_kernel<OP1, OP2, T, V, false, true, MAX>, grid, 256, 0, st, p);
-        else launch_dependent(fused_rows_kernel<OP1, OP2, T, 1, false, true, MAX>, grid, 256, 0, st, p);
-    }
+    if (stage)
+        return vec ? reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, true>)
+                   : reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, 1, true>);
+    return vec ? reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, V, false>)
+               : reinterpret_cast<const void*>(&fused_rows_kernel<OP1, OP2, T, 1, false>);
 }
 
 // red = false only with vec && stage (fused_chain_rows checks both before it launches).
@@ -368,8 +345,13 @@ static void launch_typed(bool vec, bool stage, bool red, unsigned grid, size_t s
         launch_dependent(fused_rows_kernel<OP1, OP2, T, V, true, false>, grid, 256, smem, st, p);
         return;
     }
-    if (p.is_max) launch_red<OP1, OP2, T, true>(vec, stage, grid, smem, p, st);
-    else launch_red<OP1, OP2, T, false>(vec, stage, grid, smem, p, st);
+    if (stage) {
+        if (vec) launch_dependent(fused_rows_kernel<OP1, OP2, T, V, true>, grid, 256, smem, st, p);
+        else launch_dependent(fused_rows_kernel<OP1, OP2, T, 1, true>, grid, 256, smem, st, p);
+    } else {
+        if (vec) launch_dependent(fused_rows_kernel<OP1, OP2, T, V, false>, grid, 256, 0, st, p);
+        else launch_dependent(fused_rows_kernel<OP1, OP2, T, 1, false>, grid, 256, 0, st, p);
+    }
 }
 
 template <class T>
@@ -377,7 +359,7 @@ static void launch_ops(int op1, int op2, bool vec, bool stage, bool red, unsigne
                        const FusedRowsArgs& p, cudaStream_t st, const void** fn_out) {
 #define CTB_FR(O1, O2)                                                            \
     if (op1 == O1 && op2 == O2) {                                                 \
-        if (fn_out) *fn_out = pick_kernel<O1, O2, T>(vec, stage, red, p.is_max);  \
+        if (fn_out) *fn_out = pick_kernel<O1, O2, T>(vec, stage, red);            \
         else launch_typed<O1, O2, T>(vec, stage, red, grid, smem, p, st);         \
         return;                                                                   \
     }
