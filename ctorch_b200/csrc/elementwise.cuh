@@ -160,7 +160,6 @@ __global__ void __launch_bounds__(kEwBlock) ew_flat(EwArgs p, Fn fn) {
     const bool b0 = p.stride[1][0] == 0;
     const bool b1 = NIN > 1 && p.stride[2][0] == 0;
     const bool b2 = NIN > 2 && p.stride[3][0] == 0;
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     const I0 s0 = b0 ? in0[0] : I0{};
     I1 s1{};
     I2 s2{};
@@ -202,6 +201,7 @@ __global__ void __launch_bounds__(kEwBlock) ew_flat(EwArgs p, Fn fn) {
         out[i] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, in0[b0 ? 0 : i], NIN > 1 ? in1[b1 ? 0 : i] : I1{},
                                                   NIN > 2 ? in2[b2 ? 0 : i] : I2{});
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -308,8 +308,8 @@ __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_long(EwArgs p, Fn fn) 
         ew_decode_row(p, row, NIN + 1, off);
         ew_row_segment<Fn, O, I0, I1, I2, NIN, BMASK, U>(p, fn, off, static_cast<int64_t>(s) * seg + threadIdx.x,
                                                          kEwBlock, U);
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 // Rows of kRowsMidPacks up to kRowsLongPacks packs: each warp takes tiles of 32 x U packs along
@@ -329,8 +329,8 @@ __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_mid(EwArgs p, Fn fn) {
         int64_t off[kMaxOps];
         ew_decode_row(p, row, NIN + 1, off);
         ew_row_segment<Fn, O, I0, I1, I2, NIN, BMASK, U>(p, fn, off, static_cast<int64_t>(s) * seg + lane, 32, U);
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 template <class Fn, class O, class I0, class I1, class I2, int NIN, int BMASK, int MINB>
@@ -397,8 +397,8 @@ __global__ void __launch_bounds__(kEwBlock, MINB) ew_rows_short(EwArgs p, Fn fn)
                 }
             }
         }
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -423,8 +423,8 @@ __global__ void __launch_bounds__(kEwBlock) ew_general(EwArgs p, Fn fn) {
         }
         out[off[0]] = ew_apply<Fn, O, I0, I1, I2, NIN>(fn, in0[off[1]], NIN > 1 ? in1[off[2]] : I1{},
                                                        NIN > 2 ? in2[off[3]] : I2{});
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -507,8 +507,8 @@ __global__ void __launch_bounds__(kEwBlock) ew_tiled(EwArgs p, Fn fn) {
             }
         }
         __syncthreads();
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 // Tiled with 4-element packs: the transposed input is read as packs of 4 along its unit-stride
@@ -621,8 +621,8 @@ __global__ void __launch_bounds__(TL / kTile * kEwBlock) ew_tiled4(EwArgs p, Fn 
             }
             __syncthreads();
         }
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 // ------------------------------------------------------------------------------------------------

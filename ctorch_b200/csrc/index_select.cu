@@ -50,8 +50,8 @@ __global__ void idx_validate(const I* idx, int64_t n, int64_t stride, int64_t si
             if (atomicCAS(reinterpret_cast<int*>(status), 0, 1) == 0)
                 *reinterpret_cast<long long*>(status + 2) = raw;
         }
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 template <class I>
@@ -112,8 +112,8 @@ __global__ void __launch_bounds__(256, 4) gather_rows(GatherArgs p) {
                 }
             }
         }
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 template <class I, class ET>
@@ -136,8 +136,8 @@ __global__ void __launch_bounds__(256) gather_general(GatherArgs p) {
             rem = q;
         }
         out[oo] = src[so];
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 template <class I>

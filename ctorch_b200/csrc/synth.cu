@@ -39,8 +39,8 @@ __global__ void fill_kernel(T* out, int64_t n, int dist, uint64_t key, int64_t f
             const uint64_t r = range == 0 ? h : h % range;
             out[i] = static_cast<T>(static_cast<int64_t>(static_cast<uint64_t>(a) + r));
         }
-    allow_dependents();  // the next kernel in the stream may launch while this one winds down
     }
+    allow_dependents();  // the next kernel in the stream may launch while this one winds down
 }
 
 int fill_random(const ctb_view* out, int dist, uint64_t seed, uint64_t stream_id, int64_t first,
