@@ -590,6 +590,9 @@ def run_case(args):
         fn = {"sum_rows": lambda: cb.sum(x, [1], True), "prod_rows": lambda: cb.prod(x, [1]),
               "argmax_cols": lambda: cb.argmax(x, 0), "max_cols": lambda: cb.max(x, 0),
               "sum_cols": lambda: cb.sum(x, [0])}[case]
+    elif case == "cols_bulk":  # rows of 4096 floats, too narrow for 148 strips: the bulk column kernel
+        x = device_fill(t((16384, 4096)), NORMAL, 1, 0, 0.0, 1.0)
+        fn = lambda: cb.argmax(x, 0)  # noqa: E731
     elif case == "cols_narrow":  # 256-byte rows: the flat narrow column kernel
         x = device_fill(t((1_000_000, 64)), NORMAL, 1, 0, 0.0, 1.0)
         fn = lambda: cb.argmax(x, 0)  # noqa: E731
@@ -821,7 +824,7 @@ def main():
                          "timings that the default one-GPU run adds to its line")
     ap.add_argument("--case", default=None,
                     help="profiling mode: launch one kernel (chain_rows, chain, sub, sum, argmin, step, add, relu, "
-                         "sum_rows, prod_rows, argmax_cols, max_cols, sum_cols, cols_narrow, cols_outer, argmin_rows, "
+                         "sum_rows, prod_rows, argmax_cols, max_cols, sum_cols, cols_bulk, cols_narrow, cols_outer, argmin_rows, "
                          "rows_short, tiled_f64, ew_general, red_runs, red_general, gather_general, index_select, mul_t, div_b) --warmup + --steps "
                          "times")
     ap.add_argument("--rows", type=int, default=16384, help="rows of X for --case (default 16384: 512 MiB)")

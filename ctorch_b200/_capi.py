@@ -94,6 +94,9 @@ def _load() -> ctypes.CDLL:
                                            ctypes.POINTER(ctypes.c_int),
                                            ctypes.POINTER(ctypes.c_int)]),
         "ctb_debug_fastdiv": (u64, [u64, u64]),
+        "ctb_debug_strip_geometry": (i32, [i64, i64, i64, i64, ctypes.POINTER(ctypes.c_int64),
+                                           ctypes.POINTER(ctypes.c_int64)]),
+        "ctb_debug_last_reduction_kernel": (i32, [ctypes.c_char_p, i32]),
         "ctb_debug_noalloc_fits": (i32, [sz]),
         "ctb_wait_timeouts": (i32, [ctypes.POINTER(ctypes.c_uint64)]),
         "ctb_debug_wait_timeout": (i32, [u64, ctypes.POINTER(ctypes.c_int)]),
@@ -108,6 +111,13 @@ def _load() -> ctypes.CDLL:
 
 
 lib = _load()
+
+
+def last_reduction_kernel():
+    """Name of the first kernel the calling thread's last reduction launched."""
+    buf = ctypes.create_string_buffer(64)
+    lib.ctb_debug_last_reduction_kernel(buf, 64)
+    return buf.value.decode()
 
 
 def last_error() -> str:

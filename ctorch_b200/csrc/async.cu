@@ -1,10 +1,14 @@
 // async.cu — the device counter of timed-out waits that the bulk-copy kernels report to
-// (async_copy.cuh), its C-ABI reader, and a self-test of the bounded wait.
+// (async_copy.cuh), its C-ABI reader, a self-test of the bounded wait, and the tensor maps of the
+// strip column kernel.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 #include <string>
 
 #include "async_copy.cuh"
 #include "common.cuh"
+#include "plan.cuh"
 
 namespace ctb {
 
@@ -46,6 +50,46 @@ unsigned long long* wait_timeout_counter() {
         g_counter[dev] = static_cast<unsigned long long*>(p);
     }
     return g_counter[dev];
+}
+
+namespace {
+
+// The driver's tensor-map encoder, fetched once through the runtime (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            f = nullptr;
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+}  // namespace
+
+bool encode_strip_map(RedPlan& plan, int elem_bytes) {
+    const RedArgs& a = plan.args;
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc || (elem_bytes != 4 && elem_bytes != 8) || a.strip_pk < 1) return false;
+    const int64_t vec = 16 / elem_bytes;
+    const int64_t batch = a.kept / a.N;
+    const int64_t rows = static_cast<int64_t>(kColsConsumers / a.strip_pk) * kStripRows;
+    const int64_t batch_stride = a.rank_k == 2 ? a.stride_k[0] : a.K * a.strideK;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(a.N), static_cast<cuuint64_t>(a.K),
+                                static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(a.strideK * elem_bytes),
+                                   static_cast<cuuint64_t>(batch_stride * elem_bytes)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(a.strip_pk * vec), static_cast<cuuint32_t>(rows), 1u};
+    const cuuint32_t unit[3] = {1u, 1u, 1u};
+    const CUresult r = enc(&plan.strip_map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_UINT64,
+                           3, const_cast<void*>(a.in), dims, strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 }  // namespace ctb

@@ -3,8 +3,10 @@
 //
 // A stage ring works as follows. A producer warp waits for a stage to be free (its "empty"
 // barrier), posts the bytes it is about to copy (arrive.expect_tx on the stage's "full" barrier)
-// and issues cp.async.bulk copies that complete against that barrier. Consumers wait on "full",
-// read the stage from shared memory and arrive on "empty".
+// and issues copies that complete against that barrier: bulk copies (cp.async.bulk, one
+// contiguous range each) or tensor copies (cp.async.bulk.tensor, one box of rows of a tensor
+// described by a tensor map). Consumers wait on "full", read the stage from shared memory and
+// arrive on "empty".
 //
 // Every wait here is bounded in time. A wait that runs out returns false; the kernel then counts
 // the event in a device counter (its address comes in the kernel's arguments, read on the host
@@ -12,6 +14,8 @@
 // a bound) and returns, leaving its outputs unwritten. No copy here uses cluster multicast: every
 // source is this GPU's own global memory, read by the CTA that consumes it.
 #pragma once
+
+#include <cuda.h>  // CUtensorMap
 
 #include <cstdint>
 
@@ -83,6 +87,19 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_addr(smem_dst)),
         "l"(gsrc), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Copies one box of a 3-D tensor (described by `map`, a __grid_constant__ kernel parameter) at
+// element coordinates (x, y, z) into this CTA's shared memory, row after row; completion is
+// counted on `bar`. x times the element size must be a multiple of 16 bytes; rows past the
+// tensor's extent arrive as zeros. smem_dst is 128-byte aligned.
+__device__ __forceinline__ void tensor_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z,
+                                               uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_addr(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
 }
 

@@ -44,6 +44,21 @@ int ctb_debug_plan_reduction(const ctb_view* in, const ctb_view* out, uint32_t m
     return CTB_OK;
 }
 
+int ctb_debug_strip_geometry(int64_t batch, int64_t np, int64_t pk_max, int64_t slots, int64_t* strips,
+                             int64_t* pk) {
+    int64_t s = 0, w = 0;
+    const bool ok = strip_geometry(batch, np, pk_max, slots, s, w);
+    if (strips) *strips = ok ? s : 0;
+    if (pk) *pk = ok ? w : 0;
+    return ok ? 1 : 0;
+}
+
+int ctb_debug_last_reduction_kernel(char* buf, int len) {
+    if (!buf || len <= 0) return CTB_ERR_ARGUMENT;
+    put(buf, len, last_reduction_kernel());
+    return CTB_OK;
+}
+
 uint64_t ctb_debug_fastdiv(uint64_t n, uint64_t d) { return FastDiv(d).div(n); }
 
 }  // extern "C"

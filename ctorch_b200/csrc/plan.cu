@@ -386,6 +386,35 @@ static int64_t best_split(int64_t tiles, int64_t slots, int64_t max_split) {
     return best;
 }
 
+namespace {
+thread_local const char* g_last_reduction_kernel = "";
+}
+
+void note_reduction_kernel(const char* name) { g_last_reduction_kernel = name; }
+const char* last_reduction_kernel() { return g_last_reduction_kernel; }
+
+bool strip_geometry(int64_t batch, int64_t np, int64_t pk_max, int64_t slots, int64_t& strips, int64_t& pk) {
+    if (batch < 1 || np < kStripMinPacks || pk_max < kStripMinPacks || slots < 1) return false;
+    const int64_t lo = (np + pk_max - 1) / pk_max;  // fewest strips a row can have
+    const int64_t hi = std::min(np / kStripMinPacks, lo + 4 * slots);
+    int64_t best = 0, best_cost = 0;
+    for (int64_t s = lo; s <= hi; ++s) {
+        // time of the busiest CTA, in pack-rows: its rounds of units times the widest strip
+        const int64_t cost = ((batch * s + slots - 1) / slots) * ((np + s - 1) / s);
+        if (best == 0 || cost < best_cost) {
+            best = s;
+            best_cost = cost;
+        }
+    }
+    if (best == 0) return false;
+    // an even spread of every pack-row over the slots
+    const double ideal = static_cast<double>(batch) * static_cast<double>(np) / static_cast<double>(slots);
+    if (ideal < 0.95 * static_cast<double>(best_cost)) return false;
+    strips = best;
+    pk = (np + best - 1) / best;
+    return true;
+}
+
 size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int outer_vec,
                              const RedOcc& occ) {
     RedArgs& a = plan.args;
@@ -396,6 +425,7 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
     plan.row_group = 1;
     plan.bulk_fixup = false;
     plan.runs = false;
+    plan.strip = false;
     a.split = 1;
     a.chunk = a.red;
     a.sk_q = a.sk_r = 0;
@@ -473,6 +503,23 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
             plan.grid = static_cast<unsigned>(work < slots ? work : slots);
             if (split > 1) scratch = static_cast<size_t>(a.kept * split) * state_bytes;
             break;
+        }
+        if (occ.cols_strip > 0) {
+            // whole columns per CTA: a batch row's packs cut into strips, one unit per (batch row,
+            // strip), units spread evenly over one CTA per SM
+            const int64_t vec = 16 / elem_bytes;
+            const int64_t batch = a.kept / a.N;
+            int64_t strips = 0, pk = 0;
+            if (strip_geometry(batch, a.N / vec, occ.strip_pk_max, sms * occ.cols_strip, strips, pk)) {
+                plan.strip = true;
+                plan.block = kColsThreads;
+                a.aux = FastDiv(static_cast<uint64_t>(strips));
+                a.strip_units = batch * strips;
+                a.strip_pk = static_cast<int>(pk);
+                const int64_t slots = sms * occ.cols_strip;
+                plan.grid = static_cast<unsigned>(a.strip_units < slots ? a.strip_units : slots);
+                break;
+            }
         }
         if (occ.cols_bulk > 0) {
             // Stream-K over (column tile, row): G CTAs take equal shares of the row-steps, so

@@ -5,6 +5,8 @@
 // the iteration space first and picks a kernel shaped for what is left.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (a plain struct; the encoder is fetched from the driver at run time)
+
 #include "common.cuh"
 
 namespace ctb {
@@ -113,6 +115,11 @@ struct RedArgs {
     // flattened (column tile, row) space, sk_q or sk_q + 1 of them. CTA c's partial for tile s
     // (when it shares s with other CTAs) is partial row c + s of the scratch.
     int64_t sk_q, sk_r;
+    // Strip column kernel: each batch row's N columns are cut into `aux` strips of at most
+    // strip_pk 16-byte packs; unit u = (batch row u / aux, strip u % aux); CTA c takes units
+    // c, c + grid, ... of strip_units.
+    int64_t strip_units;
+    int strip_pk;
     unsigned long long* timeouts;  // device counter of timed-out waits (async_copy.cuh)
 };
 
@@ -128,9 +135,11 @@ struct RedPlan {
     bool bulk = false;       // Outer: bulk-copy column kernel (red_cols_bulk) instead of red_outer
     bool narrow = false;     // Outer: contiguous narrow rows (red_cols_narrow) instead of red_outer
     bool bulk_fixup = false; // bulk: some column tile is shared by several CTAs (second pass)
+    bool strip = false;      // Outer: column strips read by tensor copies (red_cols_strip)
     bool runs = false;       // General, CTA per output: the innermost reduced dim is contiguous and
                              // pack-aligned, so red_runs_cta streams 16-byte packs along its runs
     int64_t bulk_tiles = 0;  // bulk: column tiles
+    CUtensorMap strip_map;   // strip: the input as a [batch, K, N] tensor of 16-byte-aligned rows
 };
 
 // Builds the kept/reduced split of `in` for the given mask and output view(s) (out2 may be null),
@@ -147,6 +156,8 @@ struct RedOcc {
     int cols_bulk = 0;  // resident bulk column CTAs per SM; 0 when that kernel cannot take the plan
     int cols_narrow = 0;  // resident narrow-column CTAs per SM; 0 when that kernel cannot take it
     int runs = 0;         // resident red_runs_cta CTAs per SM; 0 when that kernel cannot take the plan
+    int cols_strip = 0;   // resident strip column CTAs per SM; 0 when that kernel cannot take it
+    int strip_pk_max = 0; // strip: the widest strip in packs (a tensor copy's row is at most 256 elements)
 };
 
 // Narrow column kernel: 256 threads, each owning one 16-byte column group of a contiguous
@@ -163,6 +174,25 @@ constexpr int kColsRowBytes = 4096;
 constexpr int kColsRows = 8;
 constexpr int kColsThreads = kColsConsumers + 32;
 
+// Strip column kernel geometry (the same 8 consumer warps and 1 producer warp). A CTA owns a strip
+// of whole columns over all K rows, so no second pass combines partial states. Its consumer
+// threads form Q = 256 / PK row groups of PK threads (one 16-byte pack of the strip each); a
+// stage is one tensor copy of Q * kStripRows rows of the strip (at most 32 KiB), and 4 stages
+// are in flight. A tensor copy moves its box row by row, so strips narrower than
+// kStripMinPacks (192 bytes) leave the copy engine, not the HBM, as the limit (argmax over dim 0
+// of float32 on B200, 268 MB: 71.7 us at 64-byte strips, 44.3-44.9 us at 224-byte strips against
+// 49.2 us for the bulk kernel's two passes).
+constexpr int kStripStages = 4;
+constexpr int kStripRows = 8;
+constexpr int kStripStageBytes = kColsConsumers * kStripRows * 16;
+constexpr int64_t kStripMinPacks = 12;
+constexpr int64_t kStripMinK = 1024;
+
+// Strips per batch row for `batch` rows of `np` packs over `slots` CTAs: the count whose widest
+// strip times the rounds of units is least (ties to fewer strips), with strips kStripMinPacks to
+// pk_max packs wide. False when none is within 95% of an even spread of the packs over the slots.
+bool strip_geometry(int64_t batch, int64_t np, int64_t pk_max, int64_t slots, int64_t& strips, int64_t& pk);
+
 // Chooses split counts / grid for a planned reduction. `state_bytes` is the size of one partial
 // state, `outer_vec` the column-strip pack width the Outer kernel will use; returns the scratch
 // bytes the plan needs.
@@ -170,5 +200,10 @@ size_t finish_reduction_plan(RedPlan& plan, int elem_bytes, int state_bytes, int
                              const RedOcc& occ);
 
 const char* red_path_name(RedPath p);
+
+// The first kernel the calling thread's last reduction launched (a static name), for tests that
+// check which kernel a shape takes.
+void note_reduction_kernel(const char* name);
+const char* last_reduction_kernel();
 
 }  // namespace ctb

@@ -695,6 +695,165 @@ template <class R> __global__ void __launch_bounds__(32 * kColsFixGroups) red_co
 }
 
 // ------------------------------------------------------------------------------------------------
+// Column reductions by strips of whole columns (4- and 8-byte types). A unit is one strip of one
+// batch row: up to PK 16-byte packs of columns over all K rows. CTA c takes units c, c + grid, ...
+// and folds each one completely, so every output is written once, by one CTA, with no partial
+// states and no second pass.
+//
+// Warp 8 is the producer: each stage is one tensor copy of RPS = Q * kStripRows rows of the strip
+// (the box of the kernel's tensor map), landing as RPS rows of PK packs back to back. The 256
+// consumer threads form Q = 256 / PK row groups; thread (q, j) owns pack j of the strip and folds
+// rows q, q + Q, q + 2Q, ... of each stage, kStripRows of them, in increasing row order. So the
+// threads of a warp read consecutive 16-byte packs of shared memory (no bank conflicts), and after
+// the last stage the Q states of each column are combined in group order with the reducer's full
+// rule (position order for max/min, a fixed order for sums).
+
+template <class R> constexpr size_t strip_combine_bytes() {
+    return static_cast<size_t>(kColsConsumers) * (16 / sizeof(typename R::In)) * sizeof(typename R::Local);
+}
+template <class R> constexpr size_t strip_smem_bytes() {
+    return static_cast<size_t>(kStripStages) * kStripStageBytes + 2 * kStripStages * sizeof(uint64_t) +
+           strip_combine_bytes<R>();
+}
+
+template <class R>
+__global__ void __launch_bounds__(kColsThreads, 1) red_cols_strip(const __grid_constant__ CUtensorMap map, RedArgs p) {
+    dependent_wait();  // the previous kernel in the stream has completed and its writes are visible
+    using T = typename R::In;
+    using S = typename R::State;
+    using L = typename R::Local;
+    constexpr int VE = 16 / static_cast<int>(sizeof(T));  // columns per pack
+    constexpr int NS = kStripStages;
+    constexpr int M = kStripRows;
+    constexpr int kConsumerWarps = kColsConsumers / 32;
+    extern __shared__ __align__(128) unsigned char strip_smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(strip_smem + static_cast<size_t>(NS) * kStripStageBytes);
+    uint64_t* empty = full + NS;
+    L* comb = reinterpret_cast<L*>(empty + NS);
+    __shared__ volatile int failed;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kConsumerWarps);
+        }
+        mbar_fence_init();
+        failed = 0;
+    }
+    __syncthreads();
+
+    const int PK = p.strip_pk;
+    const int Q = kColsConsumers / PK;
+    const int RPS = Q * M;
+    const int64_t np = p.N / VE;
+    const int64_t strips = static_cast<int64_t>(p.aux.d);
+    const int K = static_cast<int>(p.K);  // the planner keeps K below 2^31 - 1
+    const int64_t c0 = blockIdx.x, cstep = gridDim.x;
+    if (warp == kConsumerWarps) {
+        // ---- producer
+        uint32_t g = 0;
+        bool ok = true;
+        for (int64_t u = c0; u < p.strip_units && ok; u += cstep) {
+            uint64_t b, s;
+            p.aux.divmod(static_cast<uint64_t>(u), b, s);
+            const int x = static_cast<int>(static_cast<int64_t>(s) * np / strips * VE);
+            for (int k = 0; k < K; k += RPS, ++g) {
+                const int slot = static_cast<int>(g % NS);
+                const bool w = mbar_wait(&empty[slot], ((g / NS) & 1u) ^ 1u);
+                if (!__all_sync(0xffffffffu, w)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(RPS * PK * 16));
+                    tensor_load_3d(strip_smem + static_cast<size_t>(slot) * kStripStageBytes, &map, x, k,
+                                   static_cast<int>(b), &full[slot]);
+                }
+            }
+        }
+        if (!ok && lane == 0) {
+            note_timeout(p.timeouts);
+            failed = 1;
+            // let the copies already issued land before the CTA's shared memory goes away
+            for (uint32_t i = g > static_cast<uint32_t>(NS) ? g - NS : 0u; i < g; ++i)
+                mbar_wait(&full[i % NS], (i / NS) & 1u);
+        }
+        return;
+    }
+
+    // ---- consumers
+    const int t = threadIdx.x;
+    const int q = t / PK, j = t - q * PK;
+    uint32_t g = 0;
+    for (int64_t u = c0; u < p.strip_units; u += cstep) {
+        uint64_t b, s;
+        p.aux.divmod(static_cast<uint64_t>(u), b, s);
+        const int64_t p0 = static_cast<int64_t>(s) * np / strips;
+        const int64_t p1 = (static_cast<int64_t>(s) + 1) * np / strips;
+        const bool active = q < Q && j < p1 - p0;
+        L st[VE];
+#pragma unroll
+        for (int e = 0; e < VE; ++e) st[e] = R::local_init();
+        for (int k = 0; k < K; k += RPS, ++g) {
+            const int slot = static_cast<int>(g % NS);
+            const bool w = !failed && mbar_wait(&full[slot], (g / NS) & 1u);
+            if (!__all_sync(0xffffffffu, w)) {
+                // give up on the rest: no more waits or folds, but every named barrier below is
+                // still met so that the other consumer warps finish too
+                if (lane == 0 && !failed) {
+                    note_timeout(p.timeouts);
+                    failed = 1;
+                }
+                continue;
+            }
+            const T* sb = reinterpret_cast<const T*>(strip_smem + static_cast<size_t>(slot) * kStripStageBytes) +
+                          static_cast<int64_t>(q * PK + j) * VE;
+            const int step = Q * PK * VE;  // elements from one of the thread's rows to its next
+            const int r0 = k + q;
+            if (active) {
+                if (k + RPS <= K) {
+                    Pack<T, VE> x[M];
+#pragma unroll
+                    for (int i = 0; i < M; ++i) x[i] = *reinterpret_cast<const Pack<T, VE>*>(sb + i * step);
+#pragma unroll
+                    for (int i = 0; i < M; ++i)
+#pragma unroll
+                        for (int e = 0; e < VE; ++e) R::fold_local(st[e], x[i].v[e], r0 + i * Q);
+                } else {
+                    for (int i = 0; i < M && r0 + i * Q < K; ++i) {
+                        const Pack<T, VE> x = *reinterpret_cast<const Pack<T, VE>*>(sb + i * step);
+#pragma unroll
+                        for (int e = 0; e < VE; ++e) R::fold_local(st[e], x.v[e], r0 + i * Q);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        if (u + cstep >= p.strip_units) allow_dependents();  // this CTA's last unit is read
+        // combine the row groups' states of each column in group order
+        if (active) {
+#pragma unroll
+            for (int e = 0; e < VE; ++e) comb[(q * PK + j) * VE + e] = st[e];
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kColsConsumers) : "memory");
+        const int cols = static_cast<int>(p1 - p0) * VE;
+        if (t < cols && !failed) {
+            S r = R::widen(comb[t], 0);
+            for (int g2 = 1; g2 < Q; ++g2) R::combine(r, R::widen(comb[g2 * PK * VE + t], 0));
+            int64_t o1 = 0, o2 = 0;
+            if (p.rank_k == 2) {
+                o1 = static_cast<int64_t>(b) * p.stride_o[0];
+                o2 = static_cast<int64_t>(b) * p.stride_o2[0];
+            }
+            const int64_t col = p0 * VE + t;
+            R::write(p, r, o1 + col, o2 + col);
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kColsConsumers) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
 // Narrow column reductions (4- and 8-byte types): each batch row is a contiguous [K, N] block
 // whose rows are at most 1 KiB. A CTA streams whole rows [k0, k1) of one block as
 // a flat run of packs: thread t reads pack t, t + M, t + 2M, ... (M = np * lanes, a multiple of
@@ -945,10 +1104,12 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
     switch (plan.path) {
     case RedPath::Inner:
         if (plan.warp_rows) {
+            note_reduction_kernel(plan.row_group > 1 ? "red_inner_group" : "red_inner_warp");
             if (plan.row_group == 4) launch_dependent(red_inner_group<R, 4>, plan.grid, kRedBlock, 0, st, a);
             else if (plan.row_group == 2) launch_dependent(red_inner_group<R, 2>, plan.grid, kRedBlock, 0, st, a);
             else launch_dependent(red_inner_warp<R>, plan.grid, kRedBlock, 0, st, a);
         } else {
+            note_reduction_kernel("red_inner_cta");
             launch_dependent(red_inner_cta<R>, plan.grid, kRedBlock, 0, st, a);
         }
         break;
@@ -956,11 +1117,21 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
         using T = typename R::In;
         if constexpr (sizeof(T) >= 4) {
             if (plan.narrow) {
+                note_reduction_kernel("red_cols_narrow");
                 launch_dependent(red_cols_narrow<R>, plan.grid, kNarrowBlock, 0, st, a);
                 break;
             }
         }
+        if constexpr (sizeof(T) >= 4) {
+            if (plan.strip) {
+                note_reduction_kernel("red_cols_strip");
+                launch_dependent(red_cols_strip<R>, plan.grid, kColsThreads, strip_smem_bytes<R>(), st,
+                                 plan.strip_map, a);
+                break;
+            }
+        }
         if (plan.bulk) {
+            note_reduction_kernel("red_cols_bulk");
             launch_dependent(red_cols_bulk<R>, plan.grid, kColsThreads, cols_smem_bytes(), st, a);
             if (int rc = check_launch("reduction")) return rc;
             if (plan.bulk_fixup) {
@@ -972,11 +1143,13 @@ int launch_reduction(RedPlan& plan, void* scratch, size_t scratch_bytes, size_t 
             break;
         }
         constexpr int VMAX = outer_vec<T>();
+        note_reduction_kernel("red_outer");
         if (plan.col_tile == 32 * VMAX) launch_dependent(red_outer<R, VMAX>, plan.grid, kOuterBlock, 0, st, a);
         else launch_dependent(red_outer<R, 1>, plan.grid, kOuterBlock, 0, st, a);
         break;
     }
     case RedPath::General:
+        note_reduction_kernel(plan.warp_rows ? "red_general_thread" : plan.runs ? "red_runs_cta" : "red_general_cta");
         if (plan.warp_rows) launch_dependent(red_general_thread<R>, plan.grid, kRedBlock, 0, st, a);
         else if (plan.runs) launch_dependent(red_runs_cta<R>, plan.grid, kRedBlock, 0, st, a);
         else launch_dependent(red_general_cta<R>, plan.grid, kRedBlock, 0, st, a);
@@ -1041,6 +1214,26 @@ inline bool cols_narrow_ok(const RedPlan& plan, int elem_bytes) {
     return a.K < (int64_t(1) << 31) - 1;
 }
 
+// Whether the strip column kernel can take this Outer plan: at most one batch dim, the input a
+// [batch, K, N] tensor a tensor map can describe (16-byte aligned base, row and batch strides
+// whole 16-byte multiples, batches after one another), rows of at least kStripMinK and positions
+// that fit the kernel's 32-bit row offsets. Whether the strips come out wide enough is the
+// planner's call (strip_geometry).
+inline bool cols_strip_ok(const RedPlan& plan, int elem_bytes) {
+    const RedArgs& a = plan.args;
+    if (plan.path != RedPath::Outer || a.rank_k > 2) return false;
+    if (reinterpret_cast<uintptr_t>(a.in) % 16) return false;
+    if ((a.N * elem_bytes) % 16 || (a.strideK * elem_bytes) % 16 || a.strideK < a.N) return false;
+    if (a.rank_k == 2 && ((a.stride_k[0] * elem_bytes) % 16 || a.stride_k[0] < a.K * a.strideK)) return false;
+    return a.K >= kStripMinK && a.K < (int64_t(1) << 31) - 1 && a.N < (int64_t(1) << 31) &&
+           a.kept / a.N < (int64_t(1) << 31);
+}
+
+// Encodes plan.strip_map for a planned strip reduction: the input as a [batch, K, N] tensor of
+// elem_bytes-sized elements, a box of one strip (strip_pk packs) by one stage of rows. False if the
+// driver's encoder is missing or refuses the tensor.
+bool encode_strip_map(RedPlan& plan, int elem_bytes);
+
 // Address of this device's timed-out-wait counter (async.cu); null if it cannot be had.
 unsigned long long* wait_timeout_counter();
 
@@ -1064,6 +1257,26 @@ template <class R> bool cols_bulk_ready() {
     return state[dev] == 1;
 }
 
+// Lets red_cols_strip<R> use its dynamic shared memory on the current device (once per device).
+template <class R> bool cols_strip_ready() {
+    static std::mutex mu;
+    static signed char state[64] = {};  // 0 unknown, 1 ready, -1 unavailable
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return false;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (state[dev] == 0) {
+        const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&red_cols_strip<R>),
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(strip_smem_bytes<R>()));
+        if (e != cudaSuccess) cudaGetLastError();
+        state[dev] = e == cudaSuccess ? 1 : -1;
+    }
+    return state[dev] == 1;
+}
+
 // Plans + sizes a reduction for reducer R; returns scratch bytes via `need`.
 template <class R>
 int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint32_t mask,
@@ -1078,6 +1291,16 @@ int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint
         if (cols_narrow_ok(plan, sizeof(T)))
             occ.cols_narrow = resident_ctas(reinterpret_cast<const void*>(&red_cols_narrow<R>), kNarrowBlock);
     }
+    if constexpr (sizeof(T) >= 4) {  // narrower types: 8 or 16 chains a thread, compute-bound
+        if (occ.cols_narrow == 0 && cols_strip_ok(plan, sizeof(T)) && cols_strip_ready<R>()) {
+            plan.args.timeouts = wait_timeout_counter();
+            if (plan.args.timeouts) {
+                occ.cols_strip = resident_ctas(reinterpret_cast<const void*>(&red_cols_strip<R>), kColsThreads,
+                                               strip_smem_bytes<R>());
+                occ.strip_pk_max = 256 / (16 / static_cast<int>(sizeof(T)));
+            }
+        }
+    }
     if (occ.cols_narrow == 0 && cols_bulk_ok(plan, sizeof(T)) && cols_bulk_ready<R>()) {
         plan.args.timeouts = wait_timeout_counter();
         if (plan.args.timeouts)
@@ -1091,6 +1314,10 @@ int plan_for(const ctb_view* in, const ctb_view* out, const ctb_view* out2, uint
     occ.general_cta = resident_ctas(reinterpret_cast<const void*>(&red_general_cta<R>), kRedBlock);
     occ.runs = resident_ctas(reinterpret_cast<const void*>(&red_runs_cta<R>), kRedBlock);
     need = finish_reduction_plan(plan, sizeof(T), sizeof(typename R::State), vec_ok ? V : 1, occ);
+    if (plan.strip && !encode_strip_map(plan, sizeof(T))) {
+        occ.cols_strip = 0;  // the bulk kernel (or the register kernel) takes it instead
+        need = finish_reduction_plan(plan, sizeof(T), sizeof(typename R::State), vec_ok ? V : 1, occ);
+    }
     return CTB_OK;
 }
 

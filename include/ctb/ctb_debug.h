@@ -23,6 +23,16 @@ CTB_API int ctb_debug_plan_elementwise(const ctb_view* out, const ctb_view* cons
 CTB_API int ctb_debug_plan_reduction(const ctb_view* in, const ctb_view* out, uint32_t reduce_mask,
                              char* path, int path_len, int* rank_kept, int* rank_red);
 
+/* The strip column kernel's geometry rule, without a device: for `batch` rows of `np` 16-byte
+ * packs over `slots` CTAs, with strips at most `pk_max` packs wide, 1 and the strip count and
+ * widest strip when the kernel takes the shape, else 0. */
+CTB_API int ctb_debug_strip_geometry(int64_t batch, int64_t np, int64_t pk_max, int64_t slots,
+                                     int64_t* strips, int64_t* pk);
+
+/* Copies into `buf` the name of the first kernel that the calling thread's last reduction
+ * launched ("red_cols_strip", "red_cols_bulk", "red_inner_warp", ...; "" before any). */
+CTB_API int ctb_debug_last_reduction_kernel(char* buf, int len);
+
 /* floor(n / d) through the kernels' invariant-divisor multiply (n < 2^63, d >= 1). */
 CTB_API uint64_t ctb_debug_fastdiv(uint64_t n, uint64_t d);
 

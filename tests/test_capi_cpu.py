@@ -230,3 +230,52 @@ def test_noalloc_size_check_refuses_needs_above_its_array():
                                                            view(C, out, dtype=dt), mask)
                         worst = max(worst, n)
     assert 0 < worst <= cap, worst
+
+
+def _strip(C, batch, np_, pk_max=64, slots=148):
+    s, w = ctypes.c_int64(-1), ctypes.c_int64(-1)
+    ok = C.lib.ctb_debug_strip_geometry(batch, np_, pk_max, slots, ctypes.byref(s), ctypes.byref(w))
+    return ok, s.value, w.value
+
+
+def test_strip_geometry_of_the_column_shapes():
+    """The strip column kernel's choice of strips: whole columns per CTA when the strips come out
+    at least 12 packs (192 bytes) wide and the units spread within 95% of evenly over the CTAs."""
+    C = _lib()
+    # argmax over dim 0 of [8192, 8192] float32: 2048 packs a row -> 147 strips of 13-14 packs
+    assert _strip(C, 1, 2048) == (1, 147, 14)
+    # [*, 32768] float32: 8192 packs -> 147 strips of at most 56 packs
+    assert _strip(C, 1, 8192) == (1, 147, 56)
+    # [*, 65536]: wider than one box row (64 packs) per CTA -> three rounds of 443 strips of 37
+    # packs (111 pack-rows for the busiest CTA, against 112 for two rounds of 293 strips of 56)
+    assert _strip(C, 1, 16384) == (1, 443, 37)
+    # float64 rows of 8192: 4096 packs, boxes up to 128 packs
+    assert _strip(C, 1, 4096, pk_max=128) == (1, 147, 28)
+    # two and three batch rows of 2048 packs share the CTAs
+    assert _strip(C, 2, 2048) == (1, 74, 28)
+    assert _strip(C, 3, 2048) == (1, 49, 42)
+    # [*, 4096] float32: 1024 packs cannot give 148 strips of 12 packs -> the bulk kernel
+    assert _strip(C, 1, 1024)[0] == 0
+    # narrow rows: nothing to split
+    assert _strip(C, 1000, 8)[0] == 0
+    assert _strip(C, 1, 11)[0] == 0
+
+
+def test_strip_geometry_invariants():
+    C = _lib()
+    rng = np.random.default_rng(7)
+    taken = 0
+    for _ in range(3000):
+        batch = int(rng.integers(1, 600))
+        np_ = int(rng.integers(1, 40000))
+        pk_max = int(rng.choice([64, 128]))
+        ok, s, w = _strip(C, batch, np_, pk_max)
+        if not ok:
+            assert (s, w) == (0, 0)
+            continue
+        taken += 1
+        assert 12 <= w <= pk_max and s * w >= np_ and s * (w - 1) < np_
+        units = batch * s
+        cost = -(-units // 148) * w
+        assert batch * np_ / 148 >= 0.95 * cost
+    assert taken > 100

@@ -603,14 +603,14 @@ BULK_COLS = [
 ]
 
 
-@pytest.mark.parametrize("shape,dim", BULK_COLS, ids=["x".join(map(str, s)) + f"-d{d}" for s, d in BULK_COLS])
-def test_column_reductions_through_the_bulk_copy_ring(cuda_ok, oracle, shape, dim):
+def _column_ops_against_the_oracle(oracle, rng, shape, dim, recipe=(), kernels=None):
+    """max/min with and without positions, sum and prod over `dim` of every dtype, bit-exact (sums,
+    means and float products within TOL_SUM). `kernels` maps a dtype to the first kernel its
+    max-with-positions must launch."""
     from ctorch_b200 import _capi as C
 
     import ctorch_b200 as cb
 
-    before = C.wait_timeouts()
-    rng = np.random.default_rng(_seed("bulk", shape, dim))
     for dt in (np.float32, np.float64, np.int32, np.int64, np.bool_):
         base = _rand(rng, shape, dt)
         if np.dtype(dt).kind == "i":
@@ -619,28 +619,66 @@ def test_column_reductions_through_the_bulk_copy_ring(cuda_ok, oracle, shape, di
             base = (np.round(base * 4) / 4).astype(dt)
             base.flat[::997] = np.nan
             base.flat[3::389] = -0.0
-        x, tx = _pair(base, [])
+        x, tx = _pair(base, recipe)
         name = np.dtype(dt).name
         for op in ("max", "min"):
             v, i = getattr(cb, op)(tx, dim, False)
+            if kernels and op == "max" and np.dtype(dt) in kernels:
+                assert C.last_reduction_kernel() == kernels[np.dtype(dt)], (shape, name, C.last_reduction_kernel())
             rv, ri = oracle.reduce_idx(op, x, dim, False)
             assert_bitexact(v.cpu().numpy(), rv, f"{op} values {shape} {name}")
             assert_bitexact(i.cpu().numpy(), ri, f"{op} indices {shape} {name}")
             got = getattr(cb, op)(tx, [dim], True).cpu().numpy()
             assert_bitexact(got, oracle.reduce(op, x, [dim], True), f"{op} {shape} {name}")
         if np.dtype(dt).kind == "f":
-            fx = np.nan_to_num(x, nan=0.5)
-            _, tfx = _pair(fx, [])
+            fbase = np.nan_to_num(base, nan=0.5)
+            fx, tfx = _pair(fbase, recipe)
             got = cb.sum(tfx, [dim], False).cpu().numpy()
             assert_close(got, oracle.reduce("sum", fx, [dim], False), TOL_SUM[np.dtype(dt)], f"sum {shape} {name}")
-            px = (1 + 1e-4 * fx).astype(dt)
-            _, tpx = _pair(px, [])
+            got = cb.mean(tfx, [dim], True).cpu().numpy()
+            assert_close(got, oracle.reduce("mean", fx, [dim], True), TOL_SUM[np.dtype(dt)], f"mean {shape} {name}")
+            px, tpx = _pair((1 + 1e-4 * fbase).astype(dt), recipe)
             got = cb.prod(tpx, [dim], False).cpu().numpy()
             assert_close(got, oracle.reduce("prod", px, [dim], False), TOL_SUM[np.dtype(dt)], f"prod {shape} {name}")
         else:
             got = cb.sum(tx, [dim], False).cpu().numpy()
             assert_bitexact(got, oracle.reduce("sum", x, [dim], False), f"sum {shape} {name}")
+
+
+@pytest.mark.parametrize("shape,dim", BULK_COLS, ids=["x".join(map(str, s)) + f"-d{d}" for s, d in BULK_COLS])
+def test_column_reductions_through_the_bulk_copy_ring(cuda_ok, oracle, shape, dim):
+    from ctorch_b200 import _capi as C
+
+    before = C.wait_timeouts()
+    _column_ops_against_the_oracle(oracle, np.random.default_rng(_seed("bulk", shape, dim)), shape, dim)
     assert C.wait_timeouts() == before, "a bulk-copy wait timed out"
+
+
+STRIP_COLS = [
+    # (base shape, view recipe, reduced dim, bool's kernel): column reductions the strip kernel
+    # takes for 4- and 8-byte types (rows of at least 1024, strips of at least 192 bytes over one
+    # CTA per SM); bool goes to the bulk kernel, or to the register kernel where its rows do not
+    # start on 16-byte boundaries. Row counts leave a partial last stage.
+    ((1024, 8192), [], 0, "red_cols_bulk"),
+    ((1030, 16384), [], 0, "red_cols_bulk"),
+    ((2, 1100, 8192), [], 1, "red_cols_bulk"),
+    ((3, 1024, 7104), [], 1, "red_cols_bulk"),  # 49 strips a batch row, of 36 or 37 packs
+    ((1024, 8320), [("slice", 1, 0, 8192, 1)], 0, "red_cols_bulk"),  # rows 8320 apart
+    ((1100, 8200), [("slice", 1, 8, 8200, 1)], 0, "red_outer"),  # base 8 elements in
+]
+
+
+@pytest.mark.parametrize("shape,recipe,dim,bool_kernel", STRIP_COLS,
+                         ids=["x".join(map(str, s)) + ("-view" if r else "") + f"-d{d}" for s, r, d, _ in STRIP_COLS])
+def test_column_reductions_through_the_strip_kernel(cuda_ok, oracle, shape, recipe, dim, bool_kernel):
+    from ctorch_b200 import _capi as C
+
+    before = C.wait_timeouts()
+    kernels = {np.dtype(t): "red_cols_strip" for t in (np.float32, np.float64, np.int32, np.int64)}
+    kernels[np.dtype(np.bool_)] = bool_kernel
+    _column_ops_against_the_oracle(oracle, np.random.default_rng(_seed("strip", shape, dim)), shape, dim, recipe,
+                                   kernels)
+    assert C.wait_timeouts() == before, "a tensor-copy wait timed out"
 
 
 def test_bounded_wait_times_out_and_the_device_stays_usable(cuda_ok):
