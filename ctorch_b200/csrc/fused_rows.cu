@@ -200,62 +200,52 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
     const int nv = C / V;  // whole packs per row (V == 1 when rows are not pack-aligned)
     double sum = 0.0;
 
-    for (int64_t row = warp; row < p.rows; row += nwarps) {
-        const T* ar = A + row * p.a_row_stride;
-        T* yr = Y ? Y + row * p.y_row_stride : nullptr;
-        T best = extreme_ident<T>(is_max);
-        int bidx = -1;
-        for (int v0 = lane; v0 < nv; v0 += 32 * U) {
-            Pack<T, V> xa[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int v = v0 + u * 32;
-                if (v < nv) xa[u] = load_pack<T, V>(ar + static_cast<int64_t>(v) * V);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int v = v0 + u * 32;
-                if (v < nv) {
-                    Pack<T, V> xb, xc, o;
-                    if (b_row) xb = *reinterpret_cast<const Pack<T, V>*>(B + v * V);
-                    if (!p.c_is_b && c_row) xc = *reinterpret_cast<const Pack<T, V>*>(Cc + v * V);
-#pragma unroll
-                    for (int e = 0; e < V; ++e) {
-                        const T bb = b_row ? xb.v[e] : B[0];
-                        const T cc = p.c_is_b ? bb : (c_row ? xc.v[e] : Cc[0]);
-                        const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(xa[u].v[e], bb), cc);
-                        o.v[e] = yv;
-                        if constexpr (RED) {
-                            sum = __dadd_rn(sum, static_cast<double>(yv));
-                            const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
-                            if (repl) {
-                                best = yv;
-                                bidx = v * V + e;
-                            }
-                        }
-                    }
-                    if (yr) store_pack<T, V>(yr + static_cast<int64_t>(v) * V, o);
-                }
+    // One element of the chain, folded into the row's extreme and the thread's sum.
+    auto element = [&](T xv, T bb, T cc, int j, T& best, int& bidx) -> T {
+        const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(xv, bb), cc);
+        if constexpr (RED) {
+            sum = __dadd_rn(sum, static_cast<double>(yv));
+            const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
+            if (repl) {
+                best = yv;
+                bidx = j;
             }
         }
-        // scalar tail (columns past the last whole pack)
+        return yv;
+    };
+    // Packs [v0 + 32u] of one row: compute, fold, store. The lean form (tag true) is the common
+    // case with every check hoisted out: b a staged row, c the same row, y written, and the row a
+    // whole number of batches; at 16 warps per SM the instructions per element set the pace.
+    auto do_packs = [&](auto lean_tag, const Pack<T, V>* xa, int v0, T* yr, T& best, int& bidx) {
+        constexpr bool L = decltype(lean_tag)::value;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int v = v0 + u * 32;
+            if (L || v < nv) {
+                Pack<T, V> xb, xc, o;
+                if (L || b_row) xb = *reinterpret_cast<const Pack<T, V>*>(B + v * V);
+                if (!L && !p.c_is_b && c_row) xc = *reinterpret_cast<const Pack<T, V>*>(Cc + v * V);
+#pragma unroll
+                for (int e = 0; e < V; ++e) {
+                    const T bb = (L || b_row) ? xb.v[e] : B[0];
+                    const T cc = (L || p.c_is_b) ? bb : (c_row ? xc.v[e] : Cc[0]);
+                    o.v[e] = element(xa[u].v[e], bb, cc, v * V + e, best, bidx);
+                }
+                if (L || yr) store_pack<T, V>(yr + static_cast<int64_t>(v) * V, o);
+            }
+        }
+    };
+    // The row's columns past its last whole pack, then its extreme: lanes combined with NaN first
+    // (lowest index), then the extreme value, then the lower index. A lane that saw only +-inf
+    // (the min/max identity) keeps index -1 = "empty"; a row of nothing else gives index 0.
+    auto finish_row = [&](int64_t row, const T* ar, T* yr, T& best, int& bidx) {
         for (int j = nv * V + lane; j < C; j += 32) {
             const T bb = b_row ? B[j] : B[0];
             const T cc = p.c_is_b ? bb : (c_row ? Cc[j] : Cc[0]);
-            const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(ar[j], bb), cc);
+            const T yv = element(ar[j], bb, cc, j, best, bidx);
             if (yr) yr[j] = yv;
-            if constexpr (RED) {
-                sum = __dadd_rn(sum, static_cast<double>(yv));
-                const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
-                if (repl) {
-                    best = yv;
-                    bidx = j;
-                }
-            }
         }
         if (RED && p.idx) {
-            // Combine lanes: NaN first (lowest index), then the extreme value, then the lower
-            // index. A lane that saw only +-inf (the min/max identity) keeps index -1 = "empty".
 #pragma unroll
             for (int m = 16; m >= 1; m >>= 1) {
                 const T ov = __shfl_xor_sync(0xffffffffu, best, m);
@@ -274,8 +264,83 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
                     bidx = oi;
                 }
             }
-            // every element equal to the identity (+inf for min, -inf for max): the first one wins
             if (lane == 0) p.idx[row * p.idx_stride] = bidx < 0 ? 0 : bidx;
+        }
+    };
+
+    if constexpr (V > 1 && !RED) {
+        // The chain alone (no reductions), software-pipelined over the warp's batches (U packs a
+        // lane of one row), row after row: the loads of the next batch, in this row or the next,
+        // are issued before the stores of this one, so every warp keeps reads in flight while it
+        // writes. With 16 warps per SM (the grid plan_fused picks for rows of a whole batch or
+        // more) it streams at the copy rate: y = (x - r) * r over [262144, 8192] float32 on B200,
+        // 2585 us against 2788-2802 us for the row loop below at 32 warps per SM, and a device
+        // copy of the same bytes 2578 us. The kernel with its reductions keeps the row loop:
+        // pipelined at 16 warps per SM its extra instructions (the float64 sum and the row
+        // extreme) left it issue-bound at 3.1-3.2 ms, against 2.7 ms for the row loop at 32.
+        const int per_row = nv > 32 * U ? (nv + 32 * U - 1) / (32 * U) : 1;  // batches per row
+        // the lean batch body: b a staged row, c the same row, y written, whole batches
+        const bool lean = STAGE && p.c_is_b && !p.b_bcast && Y != nullptr && nv % (32 * U) == 0;
+        const int64_t my_rows = warp < p.rows ? (p.rows - warp + nwarps - 1) / nwarps : 0;
+        const int64_t nb = my_rows * per_row;
+        int64_t row = warp, nrow = warp;
+        int k = 0, nk = 0;
+        auto advance = [&](int64_t& r, int& b) {
+            if (++b == per_row) {
+                b = 0;
+                r += nwarps;
+            }
+        };
+        auto load_batch = [&](Pack<T, V>* xa, int64_t r, int b) {
+            const T* ar = A + r * p.a_row_stride;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int v = b * 32 * U + u * 32 + lane;
+                if (lean || v < nv) xa[u] = load_pack<T, V>(ar + static_cast<int64_t>(v) * V);
+            }
+        };
+        Pack<T, V> xa[U];
+        if (nb > 0) load_batch(xa, row, 0);
+        advance(nrow, nk);
+        T best = extreme_ident<T>(is_max);
+        int bidx = -1;
+        for (int64_t t = 0; t < nb; ++t) {
+            const bool more = t + 1 < nb;
+            Pack<T, V> nx[U];
+            if (more) load_batch(nx, nrow, nk);
+            T* yr = Y ? Y + row * p.y_row_stride : nullptr;
+            const int v0 = k * 32 * U + lane;
+            if (lean) do_packs(std::true_type{}, xa, v0, yr, best, bidx);
+            else do_packs(std::false_type{}, xa, v0, yr, best, bidx);
+            if (k == per_row - 1) {
+                finish_row(row, A + row * p.a_row_stride, yr, best, bidx);
+                best = extreme_ident<T>(is_max);
+                bidx = -1;
+            }
+            if (more) {
+#pragma unroll
+                for (int u = 0; u < U; ++u) xa[u] = nx[u];
+            }
+            row = nrow;
+            k = nk;
+            advance(nrow, nk);
+        }
+    } else {
+        for (int64_t row = warp; row < p.rows; row += nwarps) {
+            const T* ar = A + row * p.a_row_stride;
+            T* yr = Y ? Y + row * p.y_row_stride : nullptr;
+            T best = extreme_ident<T>(is_max);
+            int bidx = -1;
+            for (int v0 = lane; v0 < nv; v0 += 32 * U) {
+                Pack<T, V> xa[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int v = v0 + u * 32;
+                    if (v < nv) xa[u] = load_pack<T, V>(ar + static_cast<int64_t>(v) * V);
+                }
+                do_packs(std::false_type{}, xa, v0, yr, best, bidx);
+            }
+            finish_row(row, ar, yr, best, bidx);
         }
     }
     // the next kernel in the stream may launch now (it waits for this one to complete before it
@@ -372,6 +437,9 @@ static void launch_ops(int op1, int op2, bool vec, bool stage, bool red, unsigne
 
 // Largest staged footprint (b and c rows) that still leaves room for two CTAs per SM.
 constexpr size_t kMaxStageBytes = 96 * 1024;
+// Shared memory a CTA of the pipelined loop asks for at least: two fit in an SM's 228 KiB, three
+// do not.
+constexpr size_t kPipeSmemBytes = 80 * 1024;
 
 // Validation + planning shared by the scratch query and the launch. Returns the grid.
 static int plan_fused(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
@@ -429,6 +497,13 @@ static int plan_fused(int op1, int op2, const ctb_view* a, const ctb_view* b, co
     smem = (p.c_is_b ? 1 : 2) * row_bytes;
     stage = smem <= kMaxStageBytes;
     if (!stage) smem = 0;
+    // The pipelined loop (the chain alone, rows of a whole batch or more: 32 lanes x 4 packs,
+    // 2 KiB) runs at exactly two CTAs per SM. Each kernel is a programmatic dependent of the one
+    // before, so its CTAs are placed as SMs free up: with room for a third CTA on an SM, some SMs
+    // took three and others one, and the slowest CTAs finished ~800 us after the fastest. Asking
+    // for at least kPipeSmemBytes of shared memory leaves room for two on every SM.
+    const bool whole_batch = !red && vec && C * es >= 32 * 4 * 16;
+    if (stage && whole_batch && smem < kPipeSmemBytes) smem = kPipeSmemBytes;
     if (!red && !(vec && stage)) return -1;  // the chain-only kernel needs both
     const void* fn = nullptr;
     if (dt == CTB_FLOAT32) launch_ops<float>(op1, op2, vec, stage, red, 0, smem, p, nullptr, &fn);
@@ -440,8 +515,13 @@ static int plan_fused(int op1, int op2, const ctb_view* a, const ctb_view* b, co
     // One wave of warps, each taking rows warp, warp + nwarps, ...: as many rounds as a full wave
     // needs, and just enough warps for those rounds, so that the last round is as full as the
     // others (32768 rows over a full wave of 5920 warps would leave the sixth round 53% full;
-    // 5464 warps keep it 99.7% full).
-    const int64_t wave = static_cast<int64_t>(sm_count()) * resident_ctas(fn, 256, smem) * 8;
+    // 5464 warps keep it 99.7% full). The chain alone on rows of a whole batch or more (32 lanes
+    // x 4 packs: 2 KiB) runs the pipelined loop at two CTAs (16 warps) per SM, where its loads in
+    // flight match what the HBM serves best; in standalone kernels of the same loop on
+    // [262144, 8192] float32, 24 warps per SM took 2788 us against 2596 us and 8 warps 3352 us.
+    const int resident = resident_ctas(fn, 256, smem);
+    const int64_t per_sm = whole_batch && resident > 2 ? 2 : resident;
+    const int64_t wave = static_cast<int64_t>(sm_count()) * per_sm * 8;
     const int64_t rounds = R < 1 ? 1 : (R + wave - 1) / wave;
     const int64_t warps = (R + rounds - 1) / rounds;
     const int64_t ctas = (warps + 7) / 8;

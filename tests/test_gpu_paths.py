@@ -441,6 +441,11 @@ CHAIN_ROWS = [
     (777, 64, np.float64, "min", False, True),
     (500, 130, np.float32, "min", True, True),
     (1, 5, np.float32, "max", False, True),
+    # rows of whole 16-byte packs: the pipelined loop, its batch-wise row extreme, a partial last
+    # batch (4100 floats: 1025 packs; 1030 doubles: 515 packs)
+    (2048, 2048, np.float32, "max", False, True),
+    (1000, 4100, np.float32, "min", False, True),
+    (600, 1030, np.float64, "max", False, True),
 ]
 
 
@@ -461,6 +466,8 @@ def test_chain_rows_single_pass(cuda_ok, oracle, rows, cols, dt, row_op, scalar,
         if rows > 2:
             x[1, 3:] = np.inf
             x[1, 2] = -np.inf
+        if rows > 3:  # every element a new extreme: each batch improves on the last
+            x[3, :] = np.linspace(1.0, -1.0, cols) if row_op == "min" else np.linspace(-1.0, 1.0, cols)
     r = (rng.uniform(0.5, 2.0, () if scalar else (1, cols))).astype(dt)
     tx, tr = torch.from_numpy(x).cuda(), torch.from_numpy(np.asarray(r)).cuda()
     y, k, s = cb.chain_rows(ops[0], ops[1], tx, tr, tr, row_op=row_op)
