@@ -94,6 +94,9 @@ template <class D, class S> __device__ __forceinline__ D cvt(S x) {
 // Binary functors. Float ops use the round-to-nearest intrinsics so that no mul+add pair is ever
 // contracted into an FMA (results must equal the separately-rounded CPU operations). Signed
 // integers wrap through their unsigned representation (src/ops/functors.h:39-66).
+// "No second op": the fused row kernel computes op1(x, b) alone (ctb_binary on row-broadcast rows).
+constexpr int kOpNone = -1;
+
 template <int OP> struct BinOp;
 template <> struct BinOp<CTB_ADD> {
     template <class T> __device__ __forceinline__ static T apply(T a, T b) {

@@ -140,6 +140,12 @@ template <class T> __device__ __forceinline__ T extreme_ident(bool is_max) {
     return is_max ? -std::numeric_limits<T>::infinity() : std::numeric_limits<T>::infinity();
 }
 
+// op2(op1(x, b), c), or op1(x, b) alone when OP2 is kOpNone (ctb_binary on row-broadcast rows).
+template <int OP1, int OP2, class T> __device__ __forceinline__ T chain_apply(T x, T b, T c) {
+    if constexpr (OP2 == kOpNone) return BinOp<OP1>::template apply<T>(x, b);
+    else return BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(x, b), c);
+}
+
 // STAGE: b and c are copied once per CTA into shared memory (a 0-d scalar is expanded to a row),
 // so the per-element reads of the broadcast row never hold registers across the latency of the
 // loads of a; without STAGE (rows too long for shared memory) they are read through L1.
@@ -202,7 +208,7 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(FusedRowsArgs p) {
 
     // One element of the chain, folded into the row's extreme and the thread's sum.
     auto element = [&](T xv, T bb, T cc, int j, T& best, int& bidx) -> T {
-        const T yv = BinOp<OP2>::template apply<T>(BinOp<OP1>::template apply<T>(xv, bb), cc);
+        const T yv = chain_apply<OP1, OP2, T>(xv, bb, cc);
         if constexpr (RED) {
             sum = __dadd_rn(sum, static_cast<double>(yv));
             const bool repl = (best == best) && ((yv != yv) || (is_max ? yv > best : yv < best));
@@ -432,6 +438,7 @@ static void launch_ops(int op1, int op2, bool vec, bool stage, bool red, unsigne
     CTB_FR(CTB_ADD, CTB_ADD) CTB_FR(CTB_SUB, CTB_SUB) CTB_FR(CTB_MUL, CTB_MUL) CTB_FR(CTB_DIV, CTB_DIV)
     CTB_FR(CTB_ADD, CTB_SUB) CTB_FR(CTB_ADD, CTB_DIV) CTB_FR(CTB_SUB, CTB_ADD) CTB_FR(CTB_MUL, CTB_SUB)
     CTB_FR(CTB_MUL, CTB_DIV) CTB_FR(CTB_DIV, CTB_ADD) CTB_FR(CTB_DIV, CTB_SUB) CTB_FR(CTB_DIV, CTB_MUL)
+    CTB_FR(CTB_ADD, kOpNone) CTB_FR(CTB_SUB, kOpNone) CTB_FR(CTB_MUL, kOpNone) CTB_FR(CTB_DIV, kOpNone)
 #undef CTB_FR
 }
 
@@ -445,7 +452,7 @@ constexpr size_t kPipeSmemBytes = 80 * 1024;
 static int plan_fused(int op1, int op2, const ctb_view* a, const ctb_view* b, const ctb_view* c,
                       const ctb_view* y, int row_op, const ctb_view* idx, FusedRowsArgs& p,
                       bool& vec, bool& stage, size_t& smem, unsigned& grid, bool red = true) {
-    if (op1 < CTB_ADD || op1 > CTB_DIV || op2 < CTB_ADD || op2 > CTB_DIV)
+    if (op1 < CTB_ADD || op1 > CTB_DIV || ((op2 < CTB_ADD || op2 > CTB_DIV) && !(op2 == kOpNone && !red)))
         return fail(CTB_ERR_ARGUMENT, "unknown binary op");
     if (row_op != CTB_MIN && row_op != CTB_MAX) return fail(CTB_ERR_ARGUMENT, "row_op must be CTB_MIN or CTB_MAX");
     const int dt = a->dtype;

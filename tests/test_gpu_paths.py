@@ -434,6 +434,34 @@ def test_front_door_errors(cuda_ok):
     assert torch.isnan(cb.mean(torch.ones(3, 0, device="cuda"), [1])).all()
 
 
+@pytest.mark.parametrize("shape,dt", [((16384, 8192), np.float32), ((16384, 4096), np.float64)])
+def test_row_broadcast_binaries_on_the_fused_row_kernel(cuda_ok, oracle, shape, dt):
+    """a op b with b one broadcast row over at least 16384 rows of 32 KiB or more runs the
+    software-pipelined row kernel of the chain (its second op absent): bit-exact against the oracle
+    for all four ops, NaN and infinities included, in place too, and with the operands the other
+    way round (which the row kernel does not take)."""
+    import torch
+
+    import ctorch_b200 as cb
+
+    rng = np.random.default_rng(_seed("rowbin", shape, np.dtype(dt).name))
+    a = rng.standard_normal(shape).astype(dt)
+    a.flat[::7919] = np.nan
+    a.flat[5::104729] = np.inf
+    b = rng.uniform(-2.0, 2.0, (1, shape[1])).astype(dt)
+    b[0, ::997] = 0.0
+    b[0, 3] = np.nan
+    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    for op in ("add", "sub", "mul", "div"):
+        got = getattr(cb, op)(ta, tb).cpu().numpy()
+        assert_bitexact(got, oracle.binary(op, a, b), f"{op} {shape} {np.dtype(dt).name}", nan_payload=False)
+    got = getattr(cb, "sub")(tb, ta).cpu().numpy()  # the broadcast row first: elementwise kernels
+    assert_bitexact(got, oracle.binary("sub", b, a), "row - matrix", nan_payload=False)
+    tc = ta.clone()
+    cb.sub_(tc, tb)
+    assert_bitexact(tc.cpu().numpy(), oracle.binary("sub", a, b), "sub_ in place", nan_payload=False)
+
+
 CHAIN_ROWS = [
     # (rows, cols, dtype, row_op, b scalar?, special values?)
     (4096, 8192, np.float32, "min", False, False),
